@@ -1,0 +1,374 @@
+"""Benchmark of the trnfft_b200 hot path (one JSON line on rank 0).
+
+Default workload: batched 1-D complex FFT + IFFT
+round trip, N = 1024, batch = 8192 per GPU, float32 planar re/im, entries
+N(0,1) from a seed.  One step = trnfft.fft then trnfft.ifft of the batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU runs are launched one process per GPU by torch.distributed.run;
+the batch is sharded (weak scaling: every rank transforms its own 8192 rows,
+no collective on the data path) and the step time is the maximum over ranks.
+
+Metric: GFLOP/s under the 5 N log2 N convention (two transforms per step),
+whole-job aggregate.  ``value`` is timed with device-resident inputs and
+CUDA events; ``e2e`` repeats the step through the public API with the inputs
+copied from pinned host memory and the result copied back inside the timed
+region.  L2 is flushed (256 MiB write) before every timed step.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(oracle/trnfft_oracle.py, the reference's own radix-2 path) on the host
+cores, on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+N = 1024
+BATCH = 8192
+METRIC = "batched C2C FFT GFLOP/s (5N*log2N), FFT+IFFT round trip"
+UNIT = "GFLOP/s"
+FALLBACK_HBM_GBS = 6650.0
+FLUSH_BYTES = 256 << 20
+
+
+def flops_per_step(n=N, batch=BATCH):
+    return 2 * 5.0 * n * math.log2(n) * batch
+
+
+def algorithmic_bytes_per_launch(n=N, batch=BATCH):
+    # read re+im, write re+im: 16 bytes per complex point
+    return 16.0 * n * batch
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs"), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel_key):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        v = d.get(kernel_key)
+        if isinstance(v, dict):
+            return v.get("dram_bytes_per_launch")
+    return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[2:6]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo")
+    return world, rank, local
+
+
+def allreduce_max(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle restatement of the reference's radix-2 algorithm
+# ---------------------------------------------------------------------------
+
+
+def cpu_reference_sample(rows: int, threads: int, seed: int = 0):
+    """Times fft+ifft of `rows` rows of N=1024 with the oracle on `threads` threads."""
+    from oracle import trnfft_oracle as O
+
+    rng = np.random.default_rng(seed)
+    xr = rng.standard_normal((rows, N)).astype(np.float32)
+    xi = rng.standard_normal((rows, N)).astype(np.float32)
+
+    def step(a, b):
+        yr, yi = O.fft(a, b)
+        return O.ifft(yr, yi)
+
+    t0 = time.perf_counter()
+    O.threaded_rows(step, (xr, xi), threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(budget_s: float = 10.0):
+    threads = os.cpu_count() or 1
+    rows = 512
+    cpu_reference_sample(64, threads)  # warm-up
+    done, elapsed = 0, 0.0
+    while elapsed < budget_s:
+        elapsed += cpu_reference_sample(rows, threads, seed=done)
+        done += rows
+    value = flops_per_step(N, done) / elapsed / 1e9
+    return {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"oracle/trnfft_oracle.py radix-2 fft+ifft, N={N}, {done} rows "
+                      f"(of {BATCH} per step) in {elapsed:.1f} s on {threads} threads"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    rows = 256
+    for _ in range(args.warmup):
+        cpu_reference_sample(rows, threads)
+    times = [cpu_reference_sample(rows, threads, seed=k) for k in range(args.steps)]
+    ms = 1000.0 * sum(times) / len(times) * (BATCH / rows)  # per full step of BATCH rows
+    value = flops_per_step(N, rows) / (sum(times) / len(times)) / 1e9
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"batched C2C FFT+IFFT round trip, N={N}, batch={BATCH} per GPU "
+                               "(BASELINE configs[0]); each step times a bounded sample of "
+                               f"{rows} rows and reports the rate", "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows of N={N} fft+ifft per step, oracle/trnfft_oracle.py"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+
+def run_ours(args, world, rank, local):
+    import trnfft_b200 as trnfft
+    from trnfft_b200 import ComplexTensor
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    xr = torch.randn(BATCH, N, device=dev, generator=g)
+    xi = torch.randn(BATCH, N, device=dev, generator=g)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    x = ComplexTensor(xr, xi)
+
+    def step():
+        y = trnfft.fft(x)
+        return trnfft.ifft(y)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    # kernel-level roofline: each of the two launches timed alone
+    launch_ms = []
+    st = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        for inv in (False, True):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            trnfft.ifft(x) if inv else trnfft.fft(x)
+            e1.record(st)
+            e1.synchronize()
+            launch_ms.append(e0.elapsed_time(e1))
+
+    barrier(world)
+    torch.cuda.synchronize()
+    step_ms = []
+    with ClockSampler(local if torch.cuda.device_count() > 1 else 0) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            step()
+            e1.record(st)
+            e1.synchronize()
+            step_ms.append(e0.elapsed_time(e1))
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_local = sum(step_ms) / len(step_ms)
+    ms = allreduce_max(ms_local, world)
+    value = world * flops_per_step() / (ms / 1e3) / 1e9
+
+    # end to end: pinned host inputs -> device -> fft -> ifft -> pinned host result
+    hr = torch.empty(BATCH, N, dtype=torch.float32, pin_memory=True)
+    hi = torch.empty(BATCH, N, dtype=torch.float32, pin_memory=True)
+    hr.copy_(xr.cpu())
+    hi.copy_(xi.cpu())
+    outr = torch.empty_like(hr, pin_memory=True)
+    outi = torch.empty_like(hi, pin_memory=True)
+    dr = torch.empty_like(xr)
+    di = torch.empty_like(xi)
+
+    def e2e_step():
+        dr.copy_(hr, non_blocking=True)
+        di.copy_(hi, non_blocking=True)
+        y = trnfft.ifft(trnfft.fft(ComplexTensor(dr, di)))
+        outr.copy_(y.real, non_blocking=True)
+        outi.copy_(y.imag, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        e2e_step()
+        e1.record(st)
+        e1.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1))
+    barrier(world)
+    e2e_max = allreduce_max(sum(e2e_ms) / len(e2e_ms), world)
+    e2e_value = world * flops_per_step() / (e2e_max / 1e3) / 1e9
+
+    # parity spot check of the timed path against the round trip identity
+    back = step()
+    err = float(torch.linalg.vector_norm(back.real - xr) / torch.linalg.vector_norm(xr))
+
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peaks()
+    avg_launch = sum(launch_ms) / len(launch_ms)
+    achieved = algorithmic_bytes_per_launch() / (avg_launch / 1e3) / 1e9
+    out = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"batched C2C FFT+IFFT round trip, N={N}, batch={BATCH} per GPU "
+                               "(BASELINE configs[0])",
+                   "global_batch": BATCH * world, "seq_len": N, "parallelism": f"batch-sharded x{world}",
+                   "l2": "flushed before every timed step (256 MiB write)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                     "traffic": profiled_traffic("k_c2c_n1024_b8192"),
+                     "kernel": "k_c2c<10,4> (Stockham radix 4-16-16)",
+                     "algorithmic_bytes_per_launch": algorithmic_bytes_per_launch(),
+                     "avg_launch_ms": round(avg_launch, 5)},
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "ms_per_step": round(e2e_max, 4),
+                "h2d_bytes_per_step": 2 * BATCH * N * 4, "d2h_bytes_per_step": 2 * BATCH * N * 4},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk.summary(),
+        "roundtrip_rel_l2": err,
+    }
+    if world == 1:
+        out["cpu_baseline"] = cpu_baseline(args.cpu_budget)
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,113 @@
+/*
+ * trnfft_b200 -- C ABI of the B200 (sm_100a) FFT hot path.
+ *
+ * This is the drop-in boundary underneath the Python package trnfft_b200,
+ * which mirrors the public API of trnsci/trnfft.  The reference reaches its
+ * device kernels through the Python dispatch layer trnfft/nki/dispatch.py
+ * (set_backend/_use_nki, dispatch.py:50-71) and the device ladder
+ * trnfft/fft_core.py:1063-1150; every entry point below replaces one call
+ * site of that ladder, cited beside it.
+ *
+ * Conventions
+ *   - Data are float32, planar (separate real and imaginary arrays), the
+ *     layout of trnfft.ComplexTensor (trnfft/complex.py:16-33).  Transforms
+ *     are batch-major and contiguous: transform b occupies [b*n, (b+1)*n).
+ *   - All pointers are device pointers on the plan's device.  Outputs are
+ *     allocated by the caller; no entry point allocates device memory except
+ *     trnfft_plan_create (plan tables).
+ *   - `stream` is a cudaStream_t passed as void*.  Work is enqueued on it and
+ *     the call returns without synchronising.
+ *   - Every function returns a trnfft_status; on failure
+ *     trnfft_last_error() (thread-local) describes the cause.  Nothing throws
+ *     across the boundary.
+ *   - Forward transforms use exp(-2*pi*i*j*k/n); inverse transforms use
+ *     exp(+2*pi*i*j*k/n) and are scaled by 1/n, like fft_core
+ *     (trnfft/fft_core.py:114-116, 1369-1370).
+ */
+#ifndef TRNFFT_B200_H
+#define TRNFFT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TRNFFT_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TRNFFT_API __attribute__((visibility("default")))
+#else
+#define TRNFFT_API
+#endif
+
+typedef enum {
+  TRNFFT_SUCCESS = 0,
+  TRNFFT_INVALID_VALUE = 1, /* bad size, null pointer, misaligned pointer */
+  TRNFFT_UNSUPPORTED = 2,   /* size or mode this build does not implement */
+  TRNFFT_CUDA_ERROR = 3,    /* a CUDA runtime call or kernel launch failed */
+  TRNFFT_ALLOC_FAILED = 4,  /* plan table allocation failed */
+  TRNFFT_INTERNAL = 5
+} trnfft_status;
+
+/* Algorithm chosen by a plan (trnfft/plan.py:14-16 has COOLEY_TUKEY and
+ * BLUESTEIN; the B200 build splits power-of-two sizes by whether one
+ * transform fits on chip). */
+typedef enum {
+  TRNFFT_ALG_COPY = 0,      /* n == 1 */
+  TRNFFT_ALG_STOCKHAM = 1,  /* power of two, n <= 4096: one pass over HBM */
+  TRNFFT_ALG_MULTIPASS = 2, /* power of two, n > 4096: 2-3 passes over HBM */
+  TRNFFT_ALG_BLUESTEIN = 3  /* any other n: fused chirp-z, one pass over HBM */
+} trnfft_algorithm;
+
+typedef struct trnfft_plan_s* trnfft_plan_t;
+
+/* ABI version of the loaded library (TRNFFT_B200_ABI_VERSION). */
+TRNFFT_API int trnfft_abi_version(void);
+
+/* Thread-local description of the last failure on this thread. */
+TRNFFT_API const char* trnfft_last_error(void);
+
+/* Create a plan for length-n transforms on CUDA device `device`.
+ * Replaces trnfft.plan.create_plan (trnfft/plan.py:34-46): the algorithm
+ * choice (power of two or Bluestein with padded_n = 2^bitlen(2n-2)) is the
+ * reference's, and unlike the reference the plan owns device tables
+ * (Bluestein chirp and filter spectrum).  Synchronises the device. */
+TRNFFT_API int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device);
+
+/* Release a plan and its device tables. */
+TRNFFT_API int trnfft_plan_destroy(trnfft_plan_t plan);
+
+/* Plan properties: algorithm (trnfft_algorithm), padded length (Bluestein m,
+ * else n) and the work-area bytes that trnfft_exec_c2c needs for `batch`
+ * transforms (0 when none). Replaces FFTPlan's fields (trnfft/plan.py:19-28). */
+TRNFFT_API int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* padded_n, int64_t batch,
+                      int64_t* work_bytes);
+
+/* Batched complex-to-complex transform along contiguous rows.
+ * Replaces fft_core(x, inverse) (trnfft/fft_core.py:22-50) -> _cooley_tukey
+ * (fft_core.py:53-117) / _bluestein (fft_core.py:1285-1376), reached from
+ * trnfft.fft / trnfft.ifft (trnfft/api.py:22-35).
+ * `work` is a device buffer of trnfft_plan_query's work_bytes (may be NULL
+ * when that is 0).  In-place (in == out) is allowed. */
+TRNFFT_API int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out_re,
+                    float* out_im, int64_t batch, int inverse, void* work, void* stream);
+
+/* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
+ * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex
+ * transform of the real row and keeps the first n//2+1 bins. */
+TRNFFT_API int trnfft_exec_r2c(trnfft_plan_t plan, const float* in, float* out_re, float* out_im,
+                    int64_t batch, void* work, void* stream);
+
+/* Batched complex-to-real transform: rows of n/2+1 bins -> rows of n reals,
+ * scaled by 1/n.  Replaces trnfft.irfft (trnfft/api.py:49-68): the result is
+ * the real part of the inverse transform of the Hermitian extension, so the
+ * imaginary parts of bin 0 and (even n) bin n/2 do not contribute. */
+TRNFFT_API int trnfft_exec_c2r(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out,
+                    int64_t batch, void* work, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRNFFT_B200_H */

@@ -1,0 +1,300 @@
+"""Device-side transform primitives over the C ABI, with autograd.
+
+Every function here takes CUDA float32 tensors whose last axis is the
+transform axis, launches one of the library's kernels on the current torch
+stream and returns new tensors (outputs are allocated with ``torch.empty`` on
+the input's device, so the caching allocator owns them).
+
+Autograd follows the reference's analytic adjoints
+(trnfft/nki/autograd.py:167-205): for y = fft(x), dx = n * ifft(dy); for
+y = ifft(x), dx = fft(dy) / n.  The real transforms use the matching
+adjoints (derived in each backward).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _flat(t: torch.Tensor, n: int) -> torch.Tensor:
+    t = t.contiguous()
+    return t.reshape(-1, n)
+
+
+def _check(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"trnfft_b200: {what} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise TypeError(f"trnfft_b200: {what} must be float32, got {t.dtype}")
+
+
+# ---------------------------------------------------------------------------
+# raw launches (no autograd)
+# ---------------------------------------------------------------------------
+
+
+def c2c_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    _check(xr, "real part")
+    _check(xi, "imaginary part")
+    n = xr.shape[-1]
+    shape = xr.shape
+    a = _flat(xr, n)
+    b = _flat(xi, n)
+    yr = torch.empty_like(a)
+    yi = torch.empty_like(b)
+    batch = a.shape[0]
+    if batch and n:
+        plan = _lib.device_plan(n, a.device)
+        wb = plan.work_bytes(batch)
+        work = torch.empty(wb, dtype=torch.uint8, device=a.device) if wb else None
+        _lib.call("trnfft_exec_c2c", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi),
+                  batch, int(bool(inverse)), _lib.ptr(work), _lib.stream_ptr(a.device))
+    return yr.reshape(shape), yi.reshape(shape)
+
+
+def _r2c_native(n: int) -> bool:
+    return n >= 4 and (n & (n - 1)) == 0 and n <= 8192
+
+
+def r2c_raw(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """rfft along the last axis: (..., n) real -> (..., n//2+1) complex."""
+    _check(x, "input")
+    n = x.shape[-1]
+    h = n // 2 + 1
+    lead = x.shape[:-1]
+    a = _flat(x, n)
+    batch = a.shape[0]
+    if not _r2c_native(n):
+        yr, yi = c2c_raw(a, torch.zeros_like(a), False)
+        return yr[:, :h].reshape(*lead, h), yi[:, :h].reshape(*lead, h)
+    if a.data_ptr() % 8:
+        a = a.clone()
+    yr = torch.empty(batch, h, dtype=torch.float32, device=a.device)
+    yi = torch.empty(batch, h, dtype=torch.float32, device=a.device)
+    if batch:
+        plan = _lib.device_plan(n, a.device)
+        _lib.call("trnfft_exec_r2c", plan.handle, _lib.ptr(a), _lib.ptr(yr), _lib.ptr(yi), batch,
+                  None, _lib.stream_ptr(a.device))
+    return yr.reshape(*lead, h), yi.reshape(*lead, h)
+
+
+def hermitian_extend(xr: torch.Tensor, xi: torch.Tensor, n: int):
+    """Full length-n spectrum built the way trnfft.irfft does (trnfft/api.py:54-66)."""
+    half = xr.shape[-1]
+    num_neg = n - half
+    if num_neg > max(half - 1, 0):
+        # the reference's slice assignment fails here (trnfft/api.py:64-65)
+        raise RuntimeError(
+            f"irfft: cannot rebuild a length-{n} spectrum from {half} bins "
+            f"(needs at least {n // 2 + 1})"
+        )
+    fr = torch.zeros(*xr.shape[:-1], n, dtype=xr.dtype, device=xr.device)
+    fi = torch.zeros_like(fr)
+    keep = min(half, n)
+    fr[..., :keep] = xr[..., :keep]
+    fi[..., :keep] = xi[..., :keep]
+    if n > 1 and num_neg > 0:
+        fr[..., half:] = torch.flip(xr[..., 1 : 1 + num_neg], dims=[-1])
+        fi[..., half:] = -torch.flip(xi[..., 1 : 1 + num_neg], dims=[-1])
+    return fr, fi
+
+
+def c2r_raw(xr: torch.Tensor, xi: torch.Tensor, n: int) -> torch.Tensor:
+    """irfft along the last axis: (..., h) complex -> (..., n) real."""
+    _check(xr, "real part")
+    _check(xi, "imaginary part")
+    h = xr.shape[-1]
+    lead = xr.shape[:-1]
+    if _r2c_native(n) and h == n // 2 + 1:
+        a = _flat(xr, h)
+        b = _flat(xi, h)
+        batch = a.shape[0]
+        y = torch.empty(batch, n, dtype=torch.float32, device=a.device)
+        if batch:
+            plan = _lib.device_plan(n, a.device)
+            _lib.call("trnfft_exec_c2r", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(y), batch,
+                      None, _lib.stream_ptr(a.device))
+        return y.reshape(*lead, n)
+    fr, fi = hermitian_extend(xr, xi, n)
+    yr, _ = c2c_raw(fr, fi, True)
+    return yr
+
+
+# ---------------------------------------------------------------------------
+# autograd
+# ---------------------------------------------------------------------------
+
+
+class _C2C(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xr, xi, inverse: bool):
+        ctx.inverse = inverse
+        ctx.n = xr.shape[-1]
+        return c2c_raw(xr, xi, inverse)
+
+    @staticmethod
+    def backward(ctx, gr, gi):
+        n = ctx.n
+        gr = torch.zeros_like(gr) if gr is None else gr
+        gi = torch.zeros_like(gi) if gi is None else gi
+        if ctx.inverse:
+            dr, di = c2c_raw(gr, gi, False)
+            s = 1.0 / n
+        else:
+            dr, di = c2c_raw(gr, gi, True)
+            s = float(n)
+        return dr * s, di * s, None
+
+
+class _R2C(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        ctx.n = x.shape[-1]
+        return r2c_raw(x)
+
+    @staticmethod
+    def backward(ctx, gr, gi):
+        # y_k = sum_t x_t e^{-2 pi i k t/n} for k <= n//2, so
+        # dx_t = Re sum_k (gr_k + i gi_k) e^{+2 pi i k t/n} = n * c2r(G') where
+        # G'_k = G_k / 2 except at k = 0 and 2k = n (c2r counts interior bins twice).
+        n = ctx.n
+        gr = gr.clone()
+        gi = gi.clone()
+        h = gr.shape[-1]
+        hi = h - 1 if n % 2 == 0 else h
+        gr[..., 1:hi] *= 0.5
+        gi[..., 1:hi] *= 0.5
+        return c2r_raw(gr.contiguous(), gi.contiguous(), n) * float(n)
+
+
+class _C2R(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xr, xi, n: int):
+        ctx.n = n
+        ctx.h = xr.shape[-1]
+        return c2r_raw(xr, xi, n)
+
+    @staticmethod
+    def backward(ctx, gy):
+        # y_t = (1/n)[Re X_0 + 2 sum_{0<k<n/2} Re(X_k e^{+i theta}) + Re X_{n/2} (-1)^t],
+        # so dX_k = c_k / n * rfft(dy)_k with c_k = 1 at k = 0 and 2k = n, else 2.
+        n, h = ctx.n, ctx.h
+        r, i = r2c_raw(gy.contiguous())
+        hb = r.shape[-1]
+        c = torch.full((hb,), 2.0 / n, dtype=r.dtype, device=r.device)
+        c[0] = 1.0 / n
+        if n % 2 == 0:
+            c[-1] = 1.0 / n
+        dr, di = r * c, i * c
+        di[..., 0] = 0.0
+        if n % 2 == 0:
+            di[..., -1] = 0.0
+        return dr, di, None
+
+
+def _needs_grad(*ts) -> bool:
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
+
+
+def c2c(xr, xi, inverse: bool):
+    if _needs_grad(xr, xi):
+        return _C2C.apply(xr, xi, inverse)
+    return c2c_raw(xr, xi, inverse)
+
+
+def r2c(x):
+    if _needs_grad(x):
+        n = x.shape[-1]
+        if _r2c_native(n):
+            return _R2C.apply(x)
+        h = n // 2 + 1
+        yr, yi = _C2C.apply(x, torch.zeros_like(x), False)
+        return yr[..., :h], yi[..., :h]
+    return r2c_raw(x)
+
+
+def c2r(xr, xi, n: int):
+    if _needs_grad(xr, xi):
+        if _r2c_native(n) and xr.shape[-1] == n // 2 + 1:
+            return _C2R.apply(xr, xi, n)
+        fr, fi = hermitian_extend(xr, xi, n)
+        yr, _ = _C2C.apply(fr, fi, True)
+        return yr
+    return c2r_raw(xr, xi, n)
+
+
+# ---------------------------------------------------------------------------
+# STFT / ISTFT
+# ---------------------------------------------------------------------------
+
+
+def _pad_signal(x2: torch.Tensor, p: int, pad_mode: str) -> torch.Tensor:
+    return torch.nn.functional.pad(x2.unsqueeze(1), (p, p), mode=pad_mode).squeeze(1)
+
+
+def stft(x: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool, pad_mode: str,
+         normalized: bool, onesided: bool):
+    """Framing (trnfft/api.py:310-336), transform of each frame, (..., freq, time) layout."""
+    _check(x, "input")
+    lead = x.shape[:-1]
+    L = x.shape[-1]
+    x2 = x.reshape(-1, L)
+    if center:
+        x2 = _pad_signal(x2, n_fft // 2, pad_mode)
+    frames = x2.unfold(-1, n_fft, hop) * w
+    if onesided:
+        yr, yi = r2c(frames)
+    else:
+        yr, yi = c2c(frames, torch.zeros_like(frames), False)
+    yr = yr.transpose(-2, -1)
+    yi = yi.transpose(-2, -1)
+    if normalized:
+        sc = 1.0 / (n_fft ** 0.5)
+        yr = yr * sc
+        yi = yi * sc
+    nb, nf = yr.shape[-2], yr.shape[-1]
+    return yr.reshape(*lead, nb, nf).contiguous(), yi.reshape(*lead, nb, nf).contiguous()
+
+
+def istft(sr: torch.Tensor, si: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool,
+          normalized: bool, onesided: bool, length):
+    """Inverse transform per frame and windowed overlap-add (trnfft/api.py:368-470)."""
+    if normalized:
+        sc = n_fft ** 0.5
+        sr = sr * sc
+        si = si * sc
+    lead = sr.shape[:-2]
+    fb, nf = sr.shape[-2], sr.shape[-1]
+    tr = sr.reshape(-1, fb, nf).transpose(-2, -1).contiguous()
+    ti = si.reshape(-1, fb, nf).transpose(-2, -1).contiguous()
+    if onesided:
+        frames = c2r(tr, ti, n_fft)
+    else:
+        frames, _ = c2c(tr, ti, True)
+    B = frames.shape[0]
+    exp_len = n_fft + (nf - 1) * hop
+
+    def ola(fr):  # (B, nf, n_fft) -> (B, exp_len)
+        return torch.nn.functional.fold(
+            fr.transpose(1, 2), output_size=(1, exp_len), kernel_size=(1, n_fft), stride=(1, hop)
+        ).reshape(fr.shape[0], exp_len)
+
+    out = ola(frames * w)
+    raw = ola(frames)
+    wsum = ola((w * w).expand(1, nf, n_fft).contiguous())[0]
+    mask = wsum > 1e-8
+    out = torch.where(mask, out / torch.where(mask, wsum, torch.ones_like(wsum)), raw)
+    if center:
+        p = n_fft // 2
+        out = out[..., p:]
+        if out.shape[-1] > p:
+            out = out[..., :-p] if length is None else out
+    if length is not None:
+        cur = out.shape[-1]
+        if cur > length:
+            out = out[..., :length]
+        elif cur < length:
+            out = torch.cat([out, torch.zeros(B, length - cur, dtype=out.dtype, device=out.device)], -1)
+    return out.reshape(*lead, out.shape[-1]).contiguous()

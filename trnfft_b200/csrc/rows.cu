@@ -1,0 +1,260 @@
+// Batched power-of-two transforms along contiguous rows, one whole transform
+// per group of threads (single-CTA Stockham, N <= 4096 complex / 8192 real).
+//
+// Replaces the reference's per-stage radix-2 loop (trnfft/fft_core.py:53-117)
+// and its NKI Stockham/butterfly kernels (trnfft/nki/stockham.py:55-235,
+// trnfft/nki/butterfly.py:64-141): every stage of a transform stays on chip,
+// so each element is read from HBM once and written once.
+//
+//   k_c2c  complex -> complex, forward or inverse (inverse scaled by 1/N)
+//   k_r2c  real rows of length N = 2M -> N/2+1 bins, via one M-point complex
+//          FFT of z[n] = x[2n] + i x[2n+1] and an on-chip split
+//   k_c2r  N/2+1 bins -> real rows of length N = 2M (inverse of k_r2c; the
+//          imaginary parts of bins 0 and N/2 do not contribute, as in
+//          trnfft/api.py:49-68 where only the real part of the inverse
+//          transform is returned)
+#include "fft_common.cuh"
+#include "kernels.h"
+
+namespace tfb {
+
+constexpr int kRowThreads = 256;
+
+template <int LOGN, int LOGE>
+struct RowGeom {
+  using S = Sched<LOGN, LOGE>;
+  static constexpr int G = kRowThreads / S::T;  // transforms per block
+  static constexpr int NP = spad_size(S::N);
+  static constexpr size_t smem = (size_t)G * 2 * NP * sizeof(float);
+};
+
+// ----------------------------------------------------------------------------
+template <int LOGN, int LOGE, bool INV>
+__global__ void __launch_bounds__(kRowThreads) k_c2c(RowArgs a) {
+  using S = Sched<LOGN, LOGE>;
+  using GM = RowGeom<LOGN, LOGE>;
+  extern __shared__ float sm[];
+  const int g = threadIdx.x / S::T;
+  const int j = threadIdx.x % S::T;
+  const long long t = (long long)blockIdx.x * GM::G + g;
+  const bool valid = t < a.batch;
+  const long long tt = valid ? t : 0;
+  const float* __restrict__ xr = a.xr + tt * a.in_stride;
+  const float* __restrict__ xi = a.xi + tt * a.in_stride;
+  float* __restrict__ yr = a.yr + tt * a.out_stride;
+  float* __restrict__ yi = a.yi + tt * a.out_stride;
+  const float sc = a.scale;
+
+  float vr[S::E], vi[S::E];
+  pass_load<LOGN, LOGE, 0>(j, vr, vi, [&](int i, float& r, float& m) {
+    r = valid ? __ldg(xr + i) : 0.f;
+    m = valid ? __ldg(xi + i) : 0.f;
+  });
+  auto gstore = [&](int i, float r, float m) {
+    if (valid) {
+      yr[i] = r * sc;
+      yi[i] = m * sc;
+    }
+  };
+  if constexpr (S::P == 1) {
+    pass_compute_store<LOGN, LOGE, 0, INV>(j, vr, vi, gstore);
+  } else {
+    float* sre = sm + g * 2 * GM::NP;
+    float* sim = sre + GM::NP;
+    pass_compute_store<LOGN, LOGE, 0, INV>(j, vr, vi, [&](int i, float r, float m) {
+      sre[spad(i)] = r;
+      sim[spad(i)] = m;
+    });
+    __syncthreads();
+    smem_passes<LOGN, LOGE, INV, 1, S::P - 1>(j, sre, sim);
+    pass_load<LOGN, LOGE, S::P - 1>(j, vr, vi, [&](int i, float& r, float& m) {
+      r = sre[spad(i)];
+      m = sim[spad(i)];
+    });
+    pass_compute_store<LOGN, LOGE, S::P - 1, INV>(j, vr, vi, gstore);
+  }
+}
+
+// Runs the M-point forward FFT of the packed row through all passes and
+// leaves the result in shared memory.
+template <int LOGM, int LOGE, bool INV, class Ld>
+__device__ __forceinline__ void fft_to_smem(int j, float* sre, float* sim, Ld ld) {
+  using S = Sched<LOGM, LOGE>;
+  float vr[S::E], vi[S::E];
+  pass_load<LOGM, LOGE, 0>(j, vr, vi, ld);
+  pass_compute_store<LOGM, LOGE, 0, INV>(j, vr, vi, [&](int i, float r, float m) {
+    sre[spad(i)] = r;
+    sim[spad(i)] = m;
+  });
+  __syncthreads();
+  smem_passes<LOGM, LOGE, INV, 1, S::P>(j, sre, sim);
+}
+
+// ----------------------------------------------------------------------------
+// Real -> complex, N = 2M.  Row t of x (length N) -> row t of y (H = M+1 bins).
+template <int LOGM, int LOGE>
+__global__ void __launch_bounds__(kRowThreads) k_r2c(RowArgs a) {
+  using S = Sched<LOGM, LOGE>;
+  using GM = RowGeom<LOGM, LOGE>;
+  constexpr int M = S::N;
+  constexpr int LOGN = LOGM + 1;
+  extern __shared__ float sm[];
+  const int g = threadIdx.x / S::T;
+  const int j = threadIdx.x % S::T;
+  const long long t = (long long)blockIdx.x * GM::G + g;
+  const bool valid = t < a.batch;
+  const long long tt = valid ? t : 0;
+  const float* __restrict__ x = a.xr + tt * a.in_stride;
+  float* __restrict__ yr = a.yr + tt * a.out_stride;
+  float* __restrict__ yi = a.yi + tt * a.out_stride;
+  float* sre = sm + g * 2 * GM::NP;
+  float* sim = sre + GM::NP;
+
+  fft_to_smem<LOGM, LOGE, false>(j, sre, sim, [&](int i, float& r, float& m) {
+    if (valid) {
+      const float2 v = __ldg(reinterpret_cast<const float2*>(x) + i);
+      r = v.x;
+      m = v.y;
+    } else {
+      r = 0.f;
+      m = 0.f;
+    }
+  });
+  // split: X_k = E_k + W_N^k O_k, E = (Z_k + conj Z_{M-k})/2, O = (Z_k - conj Z_{M-k})/(2i)
+  for (int k = j; k <= M; k += S::T) {
+    const int k0 = k & (M - 1);
+    const int k1 = (M - k) & (M - 1);
+    const float zr = sre[spad(k0)], zi = sim[spad(k0)];
+    const float wr = sre[spad(k1)], wi = sim[spad(k1)];
+    const float er = 0.5f * (zr + wr), ei = 0.5f * (zi - wi);
+    const float orr = 0.5f * (zi + wi), oi = 0.5f * (wr - zr);
+    const float2 w = tw_lookup(k << (kTwLog - LOGN));  // k <= M: index <= 4096 < 8192
+    if (valid) {
+      yr[k] = er + (orr * w.x - oi * w.y);
+      yi[k] = ei + (orr * w.y + oi * w.x);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Complex -> real, N = 2M.  Row t of the spectrum (bins 0..M) -> real row t.
+template <int LOGM, int LOGE>
+__global__ void __launch_bounds__(kRowThreads) k_c2r(RowArgs a) {
+  using S = Sched<LOGM, LOGE>;
+  using GM = RowGeom<LOGM, LOGE>;
+  constexpr int M = S::N;
+  constexpr int LOGN = LOGM + 1;
+  extern __shared__ float sm[];
+  const int g = threadIdx.x / S::T;
+  const int j = threadIdx.x % S::T;
+  const long long t = (long long)blockIdx.x * GM::G + g;
+  const bool valid = t < a.batch;
+  const long long tt = valid ? t : 0;
+  const float* __restrict__ xr = a.xr + tt * a.in_stride;
+  const float* __restrict__ xi = a.xi + tt * a.in_stride;
+  float* __restrict__ y = a.yr + tt * a.out_stride;
+  float* sre = sm + g * 2 * GM::NP;
+  float* sim = sre + GM::NP;
+  const float sc = a.scale;  // 1/N
+
+  // Z_k = E_k + i O_k with E_k = (X_k + conj X_{M-k})/2, O_k = (X_k - conj X_{M-k}) conj(W_N^k)/2
+  fft_to_smem<LOGM, LOGE, true>(j, sre, sim, [&](int k, float& r, float& m) {
+    if (!valid) {
+      r = 0.f;
+      m = 0.f;
+      return;
+    }
+    const int km = M - k;  // in [1, M]
+    float ar = __ldg(xr + k), ai = (k == 0) ? 0.f : __ldg(xi + k);
+    float br = __ldg(xr + km), bi = (km == M) ? 0.f : __ldg(xi + km);
+    const float er = ar + br, ei = ai - bi;      // 2 E_k
+    const float dr = ar - br, di = ai + bi;      // X_k - conj X_{M-k}
+    const float2 w = tw_lookup(k << (kTwLog - LOGN));
+    // 2 O_k = d * conj(w)
+    const float orr = dr * w.x + di * w.y;
+    const float oi = di * w.x - dr * w.y;
+    // 2 Z_k = 2E + i 2O
+    r = er - oi;
+    m = ei + orr;
+  });
+  // The loads carry 2Z; the unscaled inverse M-point transform of 2Z is 2M z = N z,
+  // so multiplying by sc = 1/N yields z = (x[2n], x[2n+1]).
+  if (valid) {
+    float2* yo = reinterpret_cast<float2*>(y);
+    for (int n = j; n < M; n += S::T) yo[n] = make_float2(sre[spad(n)] * sc, sim[spad(n)] * sc);
+  }
+}
+
+// ----------------------------------------------------------------------------
+template <int LOGN>
+struct RowLogE {
+  // values per thread; E = 16 keeps every transform <= 3 passes for N <= 4096
+  static constexpr int v = 4;
+};
+
+template <int LOGN, bool INV>
+static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st) {
+  constexpr int LE = RowLogE<LOGN>::v;
+  using GM = RowGeom<LOGN, LE>;
+  auto kern = k_c2c<LOGN, LE, INV>;
+  const size_t smem = (Sched<LOGN, LE>::P == 1) ? 0 : GM::smem;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const long long blocks = (a.batch + GM::G - 1) / GM::G;
+  kern<<<(unsigned)blocks, kRowThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int LOGM, int MODE>
+static cudaError_t launch_real_t(const RowArgs& a, cudaStream_t st) {
+  constexpr int LE = RowLogE<LOGM>::v;
+  using GM = RowGeom<LOGM, LE>;
+  auto kern = (MODE == 0) ? k_r2c<LOGM, LE> : k_c2r<LOGM, LE>;
+  const size_t smem = GM::smem;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  const long long blocks = (a.batch + GM::G - 1) / GM::G;
+  kern<<<(unsigned)blocks, kRowThreads, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st) {
+  if (a.batch <= 0) return cudaSuccess;
+#define TFB_C2C_CASE(L) \
+  case L: return inv ? launch_c2c_t<L, true>(a, st) : launch_c2c_t<L, false>(a, st);
+  switch (logn) {
+    TFB_C2C_CASE(1) TFB_C2C_CASE(2) TFB_C2C_CASE(3) TFB_C2C_CASE(4)
+    TFB_C2C_CASE(5) TFB_C2C_CASE(6) TFB_C2C_CASE(7) TFB_C2C_CASE(8)
+    TFB_C2C_CASE(9) TFB_C2C_CASE(10) TFB_C2C_CASE(11) TFB_C2C_CASE(12)
+    default: return cudaErrorInvalidValue;
+  }
+#undef TFB_C2C_CASE
+}
+
+cudaError_t launch_rows_r2c(int logm, const RowArgs& a, cudaStream_t st) {
+  if (a.batch <= 0) return cudaSuccess;
+#define TFB_R_CASE(L) case L: return launch_real_t<L, 0>(a, st);
+  switch (logm) {
+    TFB_R_CASE(1) TFB_R_CASE(2) TFB_R_CASE(3) TFB_R_CASE(4) TFB_R_CASE(5) TFB_R_CASE(6)
+    TFB_R_CASE(7) TFB_R_CASE(8) TFB_R_CASE(9) TFB_R_CASE(10) TFB_R_CASE(11) TFB_R_CASE(12)
+    default: return cudaErrorInvalidValue;
+  }
+#undef TFB_R_CASE
+}
+
+cudaError_t launch_rows_c2r(int logm, const RowArgs& a, cudaStream_t st) {
+  if (a.batch <= 0) return cudaSuccess;
+#define TFB_R_CASE(L) case L: return launch_real_t<L, 1>(a, st);
+  switch (logm) {
+    TFB_R_CASE(1) TFB_R_CASE(2) TFB_R_CASE(3) TFB_R_CASE(4) TFB_R_CASE(5) TFB_R_CASE(6)
+    TFB_R_CASE(7) TFB_R_CASE(8) TFB_R_CASE(9) TFB_R_CASE(10) TFB_R_CASE(11) TFB_R_CASE(12)
+    default: return cudaErrorInvalidValue;
+  }
+#undef TFB_R_CASE
+}
+
+}  // namespace tfb

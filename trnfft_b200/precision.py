@@ -1,0 +1,47 @@
+"""Precision-mode selection (same API as trnfft/precision.py:70-94).
+
+``"fast"`` (default) and ``"double"`` are the modes that matter on B200:
+
+* ``"fast"``: float32 kernels.  Power-of-two sizes run the Stockham kernels
+  (about 2e-7 relative L2 error against an fp64 FFT).  Bluestein sizes use a
+  chirp whose angle pi*(k^2 mod 2n)/n is reduced exactly in integers before
+  it is rounded, so the float32 pipeline reaches about 4e-7 instead of the
+  reference's 1e-4 (its float32 angle pi*k*k/n, trnfft/fft_core.py:1316-1320,
+  loses ~1e-3 rad at k ~ 4000).
+* ``"double"``: the reference promotes Bluestein to float64 for accuracy
+  (fft_core.py:1306-1309).  The float32 exact-chirp kernels already land
+  within 1e-6 of that result, so they serve this mode too.
+
+The remaining modes (``"kahan"``, ``"bf16"``, ``"bf16_refined"``, ``"ozaki"``,
+``"ozaki_hq"``) are Trainium PSUM-precision experiments of the reference
+(fft_core.py:169-545).  They are accepted so that code which sets them keeps
+working, and they run the float32 kernels.
+"""
+
+from __future__ import annotations
+
+_VALID = ("fast", "kahan", "double", "bf16", "bf16_refined", "ozaki", "ozaki_hq")
+
+_precision: str = "fast"
+
+
+def set_precision(mode: str) -> None:
+    """Set the global precision mode."""
+    global _precision
+    if mode not in _VALID:
+        raise ValueError(f"precision mode must be one of {_VALID}; got {mode!r}")
+    _precision = mode
+
+
+def get_precision() -> str:
+    """Return the current global precision mode."""
+    return _precision
+
+
+def _resolve(precision) -> str:
+    """Resolve an optional per-call precision override against the global."""
+    if precision is None:
+        return _precision
+    if precision not in _VALID:
+        raise ValueError(f"precision must be one of {_VALID} or None; got {precision!r}")
+    return precision
