@@ -14,7 +14,7 @@ Metric: GFLOP/s under the 5 N log2 N convention (two transforms per step),
 whole-job aggregate.  ``value`` is timed with device-resident inputs and
 CUDA events; ``e2e`` repeats the step through the public API with the inputs
 copied from pinned host memory and the result copied back inside the timed
-region.  L2 is flushed (256 MiB write) before every timed step.
+region.  L2 is flushed (256 MiB read sweep) before every timed step.
 
 ``--impl reference`` times the CPU restatement of the reference algorithm
 (oracle/trnfft_oracle.py, the reference's own radix-2 path) on the host
@@ -28,7 +28,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -78,58 +77,66 @@ def profiled_traffic(kernel_key):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples SM clocks and throttle reasons (NVML) while the timed region runs."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {  # nvmlClocksEventReason bits
+        "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_s: float = 0.0005):
         self.index = index
-        self.proc = None
-        self.lines = []
+        self.period = period_s
+        self.sm = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self.ok = False
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            return self
+        self._sample()
+        self.t = threading.Thread(target=self._loop, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _sample(self):
+        nv = self.nv
+        self.sm.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+        try:
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        for name, b in self.REASONS.items():
+            if bits & b:
+                self.reasons.add(name)
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.ok:
+            self._stop.set()
+            self.t.join(timeout=2)
+            self._sample()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 6:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx = float(parts[1])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[2:6]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml"}
 
 
 def dist_setup():
@@ -155,6 +162,10 @@ def allreduce_max(v: float, world: int) -> float:
     t = torch.tensor([v], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def rel_err(a, b):
+    return float(torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b))
 
 
 def barrier(world):
@@ -239,7 +250,13 @@ def run_ours(args, world, rank, local):
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     xr = torch.randn(BATCH, N, device=dev, generator=g)
     xi = torch.randn(BATCH, N, device=dev, generator=g)
-    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush_out = torch.empty(1, dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        # read-only sweep of a buffer twice the L2 size: evicts every line
+        # (dirty lines are written back here, not inside the timed kernel)
+        torch.sum(flush, dim=0, keepdim=True, out=flush_out)
     x = ComplexTensor(xr, xi)
 
     def step():
@@ -250,36 +267,46 @@ def run_ours(args, world, rank, local):
         step()
     torch.cuda.synchronize()
 
-    # kernel-level roofline: each of the two launches timed alone
-    launch_ms = []
+    # The step (and each launch alone) is captured once as a CUDA graph, so the
+    # device timing below contains no host dispatch gaps.  Before every timed
+    # replay the L2 is flushed; the flush is enqueued first so the GPU is busy
+    # while the events and the replay are queued behind it.
     st = torch.cuda.current_stream(dev)
-    for _ in range(3):
-        for inv in (False, True):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            trnfft.ifft(x) if inv else trnfft.fft(x)
-            e1.record(st)
-            e1.synchronize()
-            launch_ms.append(e0.elapsed_time(e1))
+    g_step, g_fft, g_ifft = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        y_step = step()
+    with torch.cuda.graph(g_fft):
+        y_fft = trnfft.fft(x)
+    with torch.cuda.graph(g_ifft):
+        y_ifft = trnfft.ifft(x)
+    for g in (g_step, g_fft, g_ifft):
+        g.replay()
+    torch.cuda.synchronize()
+
+    def timed(graph):
+        flush_l2()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        graph.replay()
+        e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    launch_ms = []
+    for _ in range(max(3, args.steps // 2)):
+        launch_ms.append(timed(g_fft))
+        launch_ms.append(timed(g_ifft))
 
     barrier(world)
     torch.cuda.synchronize()
-    step_ms = []
-    with ClockSampler(local if torch.cuda.device_count() > 1 else 0) as clk:
-        for _ in range(args.steps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            step()
-            e1.record(st)
-            e1.synchronize()
-            step_ms.append(e0.elapsed_time(e1))
+    with ClockSampler(local) as clk:
+        step_ms = [timed(g_step) for _ in range(args.steps)]
         torch.cuda.synchronize()
     barrier(world)
     ms_local = sum(step_ms) / len(step_ms)
     ms = allreduce_max(ms_local, world)
     value = world * flops_per_step() / (ms / 1e3) / 1e9
+    ok = rel_err(y_step.real, xr) < 1e-5 and rel_err(y_fft.real, torch.fft.fft(torch.complex(xr, xi)).real) < 1e-5
 
     # end to end: pinned host inputs -> device -> fft -> ifft -> pinned host result
     hr = torch.empty(BATCH, N, dtype=torch.float32, pin_memory=True)
@@ -314,9 +341,7 @@ def run_ours(args, world, rank, local):
     e2e_max = allreduce_max(sum(e2e_ms) / len(e2e_ms), world)
     e2e_value = world * flops_per_step() / (e2e_max / 1e3) / 1e9
 
-    # parity spot check of the timed path against the round trip identity
-    back = step()
-    err = float(torch.linalg.vector_norm(back.real - xr) / torch.linalg.vector_norm(xr))
+    err = rel_err(y_step.real, xr)
 
     if rank != 0:
         return
@@ -331,7 +356,7 @@ def run_ours(args, world, rank, local):
         "config": {"workload": f"batched C2C FFT+IFFT round trip, N={N}, batch={BATCH} per GPU "
                                "(BASELINE configs[0])",
                    "global_batch": BATCH * world, "seq_len": N, "parallelism": f"batch-sharded x{world}",
-                   "l2": "flushed before every timed step (256 MiB write)"},
+                   "l2": "flushed before every timed step (256 MiB read sweep)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": profiled_traffic("k_c2c_n1024_b8192"),
@@ -342,7 +367,8 @@ def run_ours(args, world, rank, local):
                 "h2d_bytes_per_step": 2 * BATCH * N * 4, "d2h_bytes_per_step": 2 * BATCH * N * 4},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
-        "roundtrip_rel_l2": err,
+        "roundtrip_rel_l2": err, "parity_ok": bool(ok),
+        "timing": "CUDA events around CUDA-graph replays of the step; L2 flushed before each",
     }
     if world == 1:
         out["cpu_baseline"] = cpu_baseline(args.cpu_budget)

@@ -1,0 +1,188 @@
+// Fused Bluestein (chirp-z) transform for any length n whose padded length
+// m = 2^bitlen(2n-2) is at most 16384 (n <= 8193), one transform per group of
+// threads, entirely on chip.
+//
+// Reference: trnfft/fft_core.py:1285-1376 computes
+//   y = x * chirp, zero-pad to m, FFT(y) * FFT(h), IFFT, take n, * chirp
+// with three radix-2 FFTs per call (FFT(h) is recomputed every call,
+// fft_core.py:1349-1353) and six HBM round trips of host tensors.  Here:
+//   * chirp_k = exp(-i*pi*(k^2 mod 2n)/n) is tabulated per plan in double and
+//     rounded once (the reference's float32 angle pi*k*k/n loses ~1e-3 rad at
+//     k ~ 4000, fft_core.py:1316-1320);
+//   * H = FFT_m(h)/m, h = conj(chirp) with the circular wrap of
+//     fft_core.py:1337-1345, is computed once per plan;
+//   * one kernel does premultiply -> forward m-point Stockham FFT -> * H ->
+//     inverse m-point FFT -> postmultiply, so x is read once and X written once.
+// The inverse transform uses conj(chirp) and H_inv[k] = conj(H[(m-k) mod m])
+// (FFT of conj(h)), and scales by 1/n (fft_core.py:1369-1370).
+#include "fft_common.cuh"
+#include "kernels.h"
+
+namespace tfb {
+
+template <int LOGM>
+struct BlueLogE {
+  // values per thread: E = 16 up to m = 4096, E = 32 above (<= 512 threads)
+  static constexpr int v = LOGM <= 12 ? 4 : 5;
+};
+
+template <int LOGM>
+struct BlueGeom {
+  static constexpr int LE = BlueLogE<LOGM>::v;
+  using S = Sched<LOGM, LE>;
+  static constexpr int THREADS = S::T > 256 ? S::T : 256;
+  static constexpr int G = THREADS / S::T;
+  static constexpr int MP = spad_size(S::N);
+  static constexpr size_t smem = (size_t)G * 2 * MP * sizeof(float);
+};
+
+// MODE 0: C2C, MODE 1: R2C (real rows -> n/2+1 bins), MODE 2: C2R (n/2+1 bins -> real rows)
+template <int LOGM, bool INV, int MODE>
+__global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS) k_bluestein(BlueArgs a) {
+  using GM = BlueGeom<LOGM>;
+  constexpr int LE = GM::LE;
+  using S = Sched<LOGM, LE>;
+  constexpr int M = S::N;
+  extern __shared__ float sm[];
+  const int g = threadIdx.x / S::T;
+  const int j = threadIdx.x % S::T;
+  const long long t = (long long)blockIdx.x * GM::G + g;
+  const bool valid = t < a.batch;
+  const long long tt = valid ? t : 0;
+  const int n = a.n;
+  const int half = n / 2;
+  float* sre = sm + g * 2 * GM::MP;
+  float* sim = sre + GM::MP;
+  const float2* __restrict__ chirp = a.chirp;
+  const float2* __restrict__ H = a.H;
+  const float csign = INV ? -1.f : 1.f;  // inverse uses conj(chirp)
+
+  // ---- load + premultiply (pass 0 of the forward m-point FFT)
+  float vr[S::E], vi[S::E];
+  pass_load<LOGM, LE, 0>(j, vr, vi, [&](int i, float& r, float& m) {
+    r = 0.f;
+    m = 0.f;
+    if (!valid || i >= n) return;
+    float xr, xi;
+    if constexpr (MODE == 0) {
+      xr = __ldg(a.xr + tt * n + i);
+      xi = __ldg(a.xi + tt * n + i);
+    } else if constexpr (MODE == 1) {
+      xr = __ldg(a.xr + tt * n + i);
+      xi = 0.f;
+    } else {
+      // Hermitian extension of the n/2+1 input bins (trnfft/api.py:54-66);
+      // only the real part of the result is kept, so the imaginary parts of
+      // bin 0 and (even n) bin n/2 are dropped.
+      const long long h = half + 1;
+      if (i <= half) {
+        xr = __ldg(a.xr + tt * h + i);
+        xi = (i == 0 || 2 * i == n) ? 0.f : __ldg(a.xi + tt * h + i);
+      } else {
+        xr = __ldg(a.xr + tt * h + (n - i));
+        xi = -__ldg(a.xi + tt * h + (n - i));
+      }
+    }
+    const float2 c = __ldg(chirp + i);
+    const float ci = csign * c.y;
+    r = fmaf(xr, c.x, -xi * ci);
+    m = fmaf(xr, ci, xi * c.x);
+  });
+  auto sstore = [&](int i, float r, float m) {
+    sre[spad(i)] = r;
+    sim[spad(i)] = m;
+  };
+  auto sload = [&](int i, float& r, float& m) {
+    r = sre[spad(i)];
+    m = sim[spad(i)];
+  };
+  if constexpr (S::P == 1) {
+    // single-pass forward FFT: multiply by H in the store
+    pass_compute_store<LOGM, LE, 0, false>(j, vr, vi, [&](int i, float r, float m) {
+      float2 h = __ldg(H + (INV ? ((M - i) & (M - 1)) : i));
+      if (INV) h.y = -h.y;
+      sstore(i, fmaf(r, h.x, -m * h.y), fmaf(r, h.y, m * h.x));
+    });
+  } else {
+    pass_compute_store<LOGM, LE, 0, false>(j, vr, vi, sstore);
+    __syncthreads();
+    smem_passes<LOGM, LE, false, 1, S::P - 1>(j, sre, sim);
+    pass_load<LOGM, LE, S::P - 1>(j, vr, vi, sload);
+    __syncthreads();
+    pass_compute_store<LOGM, LE, S::P - 1, false>(j, vr, vi, [&](int i, float r, float m) {
+      float2 h = __ldg(H + (INV ? ((M - i) & (M - 1)) : i));
+      if (INV) h.y = -h.y;
+      sstore(i, fmaf(r, h.x, -m * h.y), fmaf(r, h.y, m * h.x));
+    });
+  }
+  __syncthreads();
+
+  // ---- inverse m-point FFT (unscaled; 1/m is folded into H) + postmultiply
+  smem_passes<LOGM, LE, true, 0, S::P - 1>(j, sre, sim);
+  pass_load<LOGM, LE, S::P - 1>(j, vr, vi, sload);
+  const float sc = INV ? 1.f / (float)n : 1.f;
+  pass_compute_store<LOGM, LE, S::P - 1, true>(j, vr, vi, [&](int i, float r, float m) {
+    if (!valid || i >= n) return;
+    if constexpr (MODE == 1) {
+      if (i > half) return;
+    }
+    const float2 c = __ldg(chirp + i);
+    const float ci = csign * c.y;
+    const float yr = fmaf(r, c.x, -m * ci) * sc;
+    const float yi = fmaf(r, ci, m * c.x) * sc;
+    if constexpr (MODE == 0) {
+      a.yr[tt * n + i] = yr;
+      a.yi[tt * n + i] = yi;
+    } else if constexpr (MODE == 1) {
+      const long long h = half + 1;
+      a.yr[tt * h + i] = yr;
+      a.yi[tt * h + i] = yi;
+    } else {
+      a.yr[tt * n + i] = yr;
+    }
+  });
+}
+
+template <int LOGM, bool INV, int MODE>
+static cudaError_t launch_blue_t(const BlueArgs& a, cudaStream_t st) {
+  using GM = BlueGeom<LOGM>;
+  auto kern = k_bluestein<LOGM, INV, MODE>;
+  if (GM::smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
+    if (e != cudaSuccess) return e;
+  }
+  const long long blocks = (a.batch + GM::G - 1) / GM::G;
+  kern<<<(unsigned)blocks, GM::THREADS, GM::smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int LOGM>
+static cudaError_t launch_blue_m(int mode, bool inv, const BlueArgs& a, cudaStream_t st) {
+  switch (mode) {
+    case 0: return inv ? launch_blue_t<LOGM, true, 0>(a, st) : launch_blue_t<LOGM, false, 0>(a, st);
+    case 1: return launch_blue_t<LOGM, false, 1>(a, st);
+    case 2: return launch_blue_t<LOGM, true, 2>(a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_bluestein(int logm, int mode, bool inv, const BlueArgs& a, cudaStream_t st) {
+  if (a.batch <= 0) return cudaSuccess;
+  switch (logm) {
+    case 3: return launch_blue_m<3>(mode, inv, a, st);
+    case 4: return launch_blue_m<4>(mode, inv, a, st);
+    case 5: return launch_blue_m<5>(mode, inv, a, st);
+    case 6: return launch_blue_m<6>(mode, inv, a, st);
+    case 7: return launch_blue_m<7>(mode, inv, a, st);
+    case 8: return launch_blue_m<8>(mode, inv, a, st);
+    case 9: return launch_blue_m<9>(mode, inv, a, st);
+    case 10: return launch_blue_m<10>(mode, inv, a, st);
+    case 11: return launch_blue_m<11>(mode, inv, a, st);
+    case 12: return launch_blue_m<12>(mode, inv, a, st);
+    case 13: return launch_blue_m<13>(mode, inv, a, st);
+    case 14: return launch_blue_m<14>(mode, inv, a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tfb

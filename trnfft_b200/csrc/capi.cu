@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <complex>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -41,7 +42,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_init_mu;
 bool g_dev_ready[kMaxDevices];
 
-// Upload the W_8192 table to `device` (once per device, that device current).
+// Upload the W_16384 table to `device` (once per device, that device current).
 int ensure_device_tables(int device) {
   std::lock_guard<std::mutex> lk(g_init_mu);
   if (device < 0 || device >= kMaxDevices) return fail(TRNFFT_INVALID_VALUE, "device %d out of range", device);
@@ -77,6 +78,29 @@ int ilog2_exact(int64_t n) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// In-place iterative radix-2 FFT in double precision (forward sign), used
+// only at plan creation to tabulate the Bluestein filter spectrum.
+void host_fft_double(std::vector<std::complex<double>>& a) {
+  const size_t n = a.size();
+  for (size_t i = 1, j = 0; i < n; ++i) {
+    size_t bit = n >> 1;
+    for (; j & bit; bit >>= 1) j ^= bit;
+    j ^= bit;
+    if (i < j) std::swap(a[i], a[j]);
+  }
+  for (size_t len = 2; len <= n; len <<= 1) {
+    const size_t h = len / 2;
+    std::vector<std::complex<double>> w(h);
+    for (size_t k = 0; k < h; ++k) w[k] = std::polar(1.0, -2.0 * M_PI * (double)k / (double)len);
+    for (size_t i = 0; i < n; i += len)
+      for (size_t k = 0; k < h; ++k) {
+        const std::complex<double> u = a[i + k], v = a[i + k + h] * w[k];
+        a[i + k] = u + v;
+        a[i + k + h] = u - v;
+      }
+  }
+}
+
 }  // namespace
 }  // namespace tfb
 
@@ -89,7 +113,39 @@ struct trnfft_plan_s {
   int logn = -1;
   int64_t m = 0;  // Bluestein padded length
   int logm = -1;
+  float2* chirp = nullptr;  // Bluestein: n entries
+  float2* H = nullptr;      // Bluestein: m entries
 };
+
+// Bluestein tables: chirp_k = exp(-i*pi*(k^2 mod 2n)/n) (exact integer
+// reduction of the angle, then double trig) and H = FFT_m(h)/m with
+// h_j = conj(chirp_j) for j < n, h_{m-j} = conj(chirp_j) for 0 < j < n.
+static int make_bluestein_tables(trnfft_plan_s* p) {
+  const int64_t n = p->n, m = p->m;
+  std::vector<float2> c(n);
+  std::vector<std::complex<double>> cd(n), h(m, 0.0);
+  for (int64_t k = 0; k < n; ++k) {
+    const int64_t e = (k * k) % (2 * n);
+    const double ang = -M_PI * (double)e / (double)n;
+    cd[k] = std::polar(1.0, ang);
+    c[k] = make_float2((float)cd[k].real(), (float)cd[k].imag());
+  }
+  for (int64_t j = 0; j < n; ++j) h[j] = std::conj(cd[j]);
+  for (int64_t j = 1; j < n; ++j) h[m - j] = std::conj(cd[j]);
+  host_fft_double(h);
+  std::vector<float2> hf(m);
+  for (int64_t k = 0; k < m; ++k)
+    hf[k] = make_float2((float)(h[k].real() / (double)m), (float)(h[k].imag() / (double)m));
+  cudaError_t e = cudaMalloc(&p->chirp, sizeof(float2) * n);
+  if (e == cudaSuccess) e = cudaMalloc(&p->H, sizeof(float2) * m);
+  if (e != cudaSuccess) return fail(TRNFFT_ALLOC_FAILED, "plan_create: %s", cudaGetErrorString(e));
+  e = cudaMemcpy(p->chirp, c.data(), sizeof(float2) * n, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(p->H, hf.data(), sizeof(float2) * m, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "plan_create: uploading Bluestein tables");
+  return TRNFFT_SUCCESS;
+}
+
+static constexpr int kMaxBluesteinLogM = 14;
 
 extern "C" {
 
@@ -127,6 +183,13 @@ int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device) {
     while (v >> bl) ++bl;
     p->m = int64_t(1) << bl;
     p->logm = bl;
+    if (bl <= kMaxBluesteinLogM) {
+      int rc2 = make_bluestein_tables(p);
+      if (rc2) {
+        trnfft_plan_destroy(p);
+        return rc2;
+      }
+    }
   }
   *plan = p;
   return TRNFFT_SUCCESS;
@@ -134,6 +197,11 @@ int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device) {
 
 int trnfft_plan_destroy(trnfft_plan_t plan) {
   if (!plan) return TRNFFT_SUCCESS;
+  if (plan->chirp || plan->H) {
+    DeviceGuard g(plan->device);
+    if (plan->chirp) cudaFree(plan->chirp);
+    if (plan->H) cudaFree(plan->H);
+  }
   delete plan;
   return TRNFFT_SUCCESS;
 }
@@ -182,6 +250,14 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
       e = launch_rows_c2c(plan->logn, inverse != 0, a, st);
       break;
     }
+    case TRNFFT_ALG_BLUESTEIN: {
+      if (!plan->H)
+        return fail(TRNFFT_UNSUPPORTED, "exec_c2c: Bluestein length n=%lld (padded %lld) above the fused "
+                    "kernel's limit n <= 8193", (long long)n, (long long)plan->m);
+      BlueArgs a{in_re, in_im, out_re, out_im, batch, (int)n, plan->chirp, plan->H};
+      e = launch_bluestein(plan->logm, 0, inverse != 0, a, st);
+      break;
+    }
     default:
       return fail(TRNFFT_UNSUPPORTED, "exec_c2c: n=%lld not supported yet", (long long)n);
   }
@@ -206,6 +282,11 @@ int trnfft_exec_r2c(trnfft_plan_t plan, const float* in, float* out_re, float* o
     if (rc) return rc;
     RowArgs a{in, nullptr, out_re, out_im, batch, n, n / 2 + 1, 1.0f};
     e = launch_rows_r2c(plan->logn - 1, a, st);
+  } else if (plan->algorithm == TRNFFT_ALG_BLUESTEIN && plan->H) {
+    int rc = check_ptrs("exec_r2c", {in, out_re, out_im}, 4);
+    if (rc) return rc;
+    BlueArgs a{in, nullptr, out_re, out_im, batch, (int)n, plan->chirp, plan->H};
+    e = launch_bluestein(plan->logm, 1, false, a, st);
   } else {
     return fail(TRNFFT_UNSUPPORTED, "exec_r2c: n=%lld not supported yet", (long long)n);
   }
@@ -230,6 +311,11 @@ int trnfft_exec_c2r(trnfft_plan_t plan, const float* in_re, const float* in_im, 
     if (rc) return rc;
     RowArgs a{in_re, in_im, out, nullptr, batch, n / 2 + 1, n, (float)(1.0 / (double)n)};
     e = launch_rows_c2r(plan->logn - 1, a, st);
+  } else if (plan->algorithm == TRNFFT_ALG_BLUESTEIN && plan->H) {
+    int rc = check_ptrs("exec_c2r", {in_re, in_im, out}, 4);
+    if (rc) return rc;
+    BlueArgs a{in_re, in_im, out, nullptr, batch, (int)n, plan->chirp, plan->H};
+    e = launch_bluestein(plan->logm, 2, true, a, st);
   } else {
     return fail(TRNFFT_UNSUPPORTED, "exec_c2r: n=%lld not supported yet", (long long)n);
   }

@@ -135,12 +135,12 @@ __device__ __forceinline__ void dft_reg(float (&re)[R], float (&im)[R]) {
 }
 
 // ---------------------------------------------------------------------------
-// Twiddle table W_8192^i = exp(-2*pi*i*i/8192), i in [0, 8192), computed in
-// double on the host and copied to every device once (a file-scope device
-// array, so no allocation).  W_N^j for any N = 2^l <= 8192 is
-// W_8192^(j << (13 - l)).
+// Twiddle table W_16384^i = exp(-2*pi*i*i/16384), i in [0, 16384), computed
+// in double on the host and copied to every device once (a file-scope device
+// array, so no allocation).  W_N^j for any N = 2^l <= 16384 is
+// W_16384^(j << (14 - l)).
 // ---------------------------------------------------------------------------
-constexpr int kTwLog = 13;
+constexpr int kTwLog = 14;
 constexpr int kTwN = 1 << kTwLog;
 extern __device__ float2 g_tw[kTwN];
 
@@ -211,14 +211,28 @@ __device__ __forceinline__ void pass_compute_store(int j, float (&vr)[Sched<LOGN
       ai[r] = vi[q * R + r];
     }
     if constexpr (NS > 1) {
-      // W_{NS*R}^{k*r} = W_8192^{(k*r) << (13 - LNS - LR)}
+      // W_{NS*R}^{k*r} = W_16384^{(k*r) << (14 - LNS - LR)}.  The power-of-two
+      // exponents r = 1, 2, 4, ... come from the table; every other r is the
+      // product of the twiddle of its highest set bit and an already formed
+      // twiddle (at most popcount(r)-1 roundings deep).
+      float wr[R], wi[R];
+      wr[0] = 1.f;
+      wi[0] = 0.f;
 #pragma unroll
       for (int r = 1; r < R; ++r) {
-        const float2 w = tw_lookup((k * r) << (kTwLog - LNS - LR));
-        const float wi = INV ? -w.y : w.y;
+        const int hb = 1 << (31 - __clz(r));
+        if (hb == r) {
+          const float2 w = tw_lookup((k * r) << (kTwLog - LNS - LR));
+          wr[r] = w.x;
+          wi[r] = INV ? -w.y : w.y;
+        } else {
+          const int lo = r - hb;
+          wr[r] = fmaf(wr[hb], wr[lo], -wi[hb] * wi[lo]);
+          wi[r] = fmaf(wr[hb], wi[lo], wi[hb] * wr[lo]);
+        }
         const float xr = ar[r], xi = ai[r];
-        ar[r] = fmaf(xr, w.x, -xi * wi);
-        ai[r] = fmaf(xr, wi, xi * w.x);
+        ar[r] = fmaf(xr, wr[r], -xi * wi[r]);
+        ai[r] = fmaf(xr, wi[r], xi * wr[r]);
       }
     }
     dft_reg<R, INV>(ar, ai);

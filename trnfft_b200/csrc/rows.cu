@@ -16,6 +16,8 @@
 #include "fft_common.cuh"
 #include "kernels.h"
 
+#include <cstdlib>
+
 namespace tfb {
 
 constexpr int kRowThreads = 256;
@@ -23,14 +25,16 @@ constexpr int kRowThreads = 256;
 template <int LOGN, int LOGE>
 struct RowGeom {
   using S = Sched<LOGN, LOGE>;
+  static_assert(S::T <= kRowThreads && kRowThreads % S::T == 0,
+                "one transform must fit in one block of kRowThreads threads");
   static constexpr int G = kRowThreads / S::T;  // transforms per block
   static constexpr int NP = spad_size(S::N);
   static constexpr size_t smem = (size_t)G * 2 * NP * sizeof(float);
 };
 
 // ----------------------------------------------------------------------------
-template <int LOGN, int LOGE, bool INV>
-__global__ void __launch_bounds__(kRowThreads) k_c2c(RowArgs a) {
+template <int LOGN, int LOGE, bool INV, int MINB = 1>
+__global__ void __launch_bounds__(kRowThreads, MINB) k_c2c(RowArgs a) {
   using S = Sched<LOGN, LOGE>;
   using GM = RowGeom<LOGN, LOGE>;
   extern __shared__ float sm[];
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kRowThreads) k_r2c(RowArgs a) {
     const float wr = sre[spad(k1)], wi = sim[spad(k1)];
     const float er = 0.5f * (zr + wr), ei = 0.5f * (zi - wi);
     const float orr = 0.5f * (zi + wi), oi = 0.5f * (wr - zr);
-    const float2 w = tw_lookup(k << (kTwLog - LOGN));  // k <= M: index <= 4096 < 8192
+    const float2 w = tw_lookup(k << (kTwLog - LOGN));  // k <= M = N/2: index < table size
     if (valid) {
       yr[k] = er + (orr * w.x - oi * w.y);
       yi[k] = ei + (orr * w.y + oi * w.x);
@@ -186,17 +190,20 @@ __global__ void __launch_bounds__(kRowThreads) k_c2r(RowArgs a) {
 }
 
 // ----------------------------------------------------------------------------
-template <int LOGN>
-struct RowLogE {
-  // values per thread; E = 16 keeps every transform <= 3 passes for N <= 4096
-  static constexpr int v = 4;
+// Row-kernel tuning variants (values per thread E = 2^LOGE, min resident
+// blocks per SM).  Variant 0 is the default; the others are selectable with
+// the environment variable TRNFFT_B200_ROW_VARIANT for measurement.
+template <int LOGE_, int MINB_>
+struct RowVar {
+  static constexpr int LOGE = LOGE_;
+  static constexpr int MINB = MINB_;
 };
 
-template <int LOGN, bool INV>
-static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st) {
-  constexpr int LE = RowLogE<LOGN>::v;
+template <int LOGN, bool INV, class V>
+static cudaError_t launch_c2c_v(const RowArgs& a, cudaStream_t st) {
+  constexpr int LE = V::LOGE;
   using GM = RowGeom<LOGN, LE>;
-  auto kern = k_c2c<LOGN, LE, INV>;
+  auto kern = k_c2c<LOGN, LE, INV, V::MINB>;
   const size_t smem = (Sched<LOGN, LE>::P == 1) ? 0 : GM::smem;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -206,6 +213,25 @@ static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st) {
   kern<<<(unsigned)blocks, kRowThreads, smem, st>>>(a);
   return cudaGetLastError();
 }
+
+template <int LOGN, bool INV>
+static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st, int variant) {
+  if constexpr (LOGN >= 8) {
+    switch (variant) {
+      case 1: return launch_c2c_v<LOGN, INV, RowVar<4, 3>>(a, st);
+      case 2: return launch_c2c_v<LOGN, INV, RowVar<5, 1>>(a, st);
+      case 3: return launch_c2c_v<LOGN, INV, RowVar<5, 2>>(a, st);
+      case 5: return launch_c2c_v<LOGN, INV, RowVar<4, 2>>(a, st);
+      default: break;
+    }
+  }
+  return launch_c2c_v<LOGN, INV, RowVar<4, 1>>(a, st);
+}
+
+template <int LOGN>
+struct RowLogE {
+  static constexpr int v = 4;
+};
 
 template <int LOGM, int MODE>
 static cudaError_t launch_real_t(const RowArgs& a, cudaStream_t st) {
@@ -224,8 +250,12 @@ static cudaError_t launch_real_t(const RowArgs& a, cudaStream_t st) {
 
 cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st) {
   if (a.batch <= 0) return cudaSuccess;
+  static const int variant = [] {
+    const char* v = getenv("TRNFFT_B200_ROW_VARIANT");
+    return v ? atoi(v) : 0;
+  }();
 #define TFB_C2C_CASE(L) \
-  case L: return inv ? launch_c2c_t<L, true>(a, st) : launch_c2c_t<L, false>(a, st);
+  case L: return inv ? launch_c2c_t<L, true>(a, st, variant) : launch_c2c_t<L, false>(a, st, variant);
   switch (logn) {
     TFB_C2C_CASE(1) TFB_C2C_CASE(2) TFB_C2C_CASE(3) TFB_C2C_CASE(4)
     TFB_C2C_CASE(5) TFB_C2C_CASE(6) TFB_C2C_CASE(7) TFB_C2C_CASE(8)
