@@ -360,7 +360,7 @@ def run_ours(args, world, rank, local):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": profiled_traffic("k_c2c_n1024_b8192"),
-                     "kernel": "k_c2c<10,4> (Stockham radix 4-16-16)",
+                     "kernel": "k_c2c<10,5> (Stockham radix 32-32)",
                      "algorithmic_bytes_per_launch": algorithmic_bytes_per_launch(),
                      "avg_launch_ms": round(avg_launch, 5)},
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "ms_per_step": round(e2e_max, 4),

@@ -75,6 +75,13 @@ TRNFFT_API const char* trnfft_last_error(void);
  * (Bluestein chirp and filter spectrum).  Synchronises the device. */
 TRNFFT_API int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device);
 
+/* Device status word of the library's kernels on `device`: 0 when all is
+ * well, 1 when a kernel gave up a bounded wait for its own bulk copies
+ * (it then skips its remaining work instead of hanging).  With clear != 0
+ * the word is reset.  Synchronous.  No counterpart in the reference (whose
+ * kernels have no device-side waits). */
+TRNFFT_API int trnfft_device_status(int device, int* status, int clear);
+
 /* Release a plan and its device tables. */
 TRNFFT_API int trnfft_plan_destroy(trnfft_plan_t plan);
 

@@ -148,3 +148,24 @@ def test_autograd_fft_and_rfft():
     (y2 * torch.arange(128, device="cuda")).sum().backward()
     assert rel_l2(host(sr.grad), host(tr.grad)) < 1e-5
     assert rel_l2(host(si.grad), host(ti.grad)) < 1e-5
+
+
+@pytest.mark.parametrize("n", [64, 1024, 4096])
+def test_c2c_misaligned_planes_take_plain_kernel(n):
+    """Planes that are not 16-byte aligned cannot feed bulk copies; the plain
+    row kernel handles them with the same results."""
+    from trnfft_b200 import _lib
+
+    rng = np.random.default_rng(n)
+    b = 37
+    xr = rng.standard_normal((b, n)).astype(np.float32)
+    xi = rng.standard_normal((b, n)).astype(np.float32)
+    br = torch.empty(b * n + 1, device="cuda")[1:].view(b, n)
+    bi = torch.empty(b * n + 1, device="cuda")[1:].view(b, n)
+    br.copy_(cuda(xr))
+    bi.copy_(cuda(xi))
+    y = trnfft.fft(ComplexTensor(br, bi))
+    er, ei = O.fft(xr, xi)
+    assert rel_l2(cplx(y), er + 1j * ei) < TOL
+    torch.cuda.synchronize()
+    assert _lib.device_status(torch.cuda.current_device()) == 0

@@ -39,6 +39,7 @@ SIGNATURES = {
     "trnfft_last_error": (ctypes.c_char_p, []),
     "trnfft_plan_create": (_INT, [ctypes.POINTER(_P), _I64, _INT]),
     "trnfft_plan_destroy": (_INT, [_P]),
+    "trnfft_device_status": (_INT, [_INT, ctypes.POINTER(_INT), _INT]),
     "trnfft_plan_query": (_INT, [_P, ctypes.POINTER(_INT), ctypes.POINTER(_I64), _I64, ctypes.POINTER(_I64)]),
     "trnfft_exec_c2c": (_INT, [_P, _P, _P, _P, _P, _I64, _INT, _P, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
@@ -90,6 +91,13 @@ def call(name: str, *args) -> None:
         if rc == INVALID_VALUE:
             raise ValueError(f"{name}: {msg}")
         raise TrnfftError(name, rc, msg)
+
+
+def device_status(device_index: int, clear: bool = True) -> int:
+    """Read (and by default clear) the kernels' device status word (0 = ok)."""
+    v = ctypes.c_int()
+    call("trnfft_device_status", int(device_index), ctypes.byref(v), int(bool(clear)))
+    return v.value
 
 
 def ptr(t: torch.Tensor | None):

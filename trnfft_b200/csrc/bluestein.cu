@@ -1,5 +1,5 @@
 // Fused Bluestein (chirp-z) transform for any length n whose padded length
-// m = 2^bitlen(2n-2) is at most 16384 (n <= 8193), one transform per group of
+// m = 2^bitlen(2n-2) is at most 16384 (n <= 8192), one transform per group of
 // threads, entirely on chip.
 //
 // Reference: trnfft/fft_core.py:1285-1376 computes
@@ -32,8 +32,8 @@ struct BlueGeom {
   using S = Sched<LOGM, LE>;
   static constexpr int THREADS = S::T > 256 ? S::T : 256;
   static constexpr int G = THREADS / S::T;
-  static constexpr int MP = spad_size(S::N);
-  static constexpr size_t smem = (size_t)G * 2 * MP * sizeof(float);
+  static constexpr int MP = S::NP;
+  static constexpr size_t smem = (size_t)G * MP * sizeof(float2);
 };
 
 // MODE 0: C2C, MODE 1: R2C (real rows -> n/2+1 bins), MODE 2: C2R (n/2+1 bins -> real rows)
@@ -51,8 +51,7 @@ __global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS) k_bluestein(BlueArgs 
   const long long tt = valid ? t : 0;
   const int n = a.n;
   const int half = n / 2;
-  float* sre = sm + g * 2 * GM::MP;
-  float* sim = sre + GM::MP;
+  float2* sb = reinterpret_cast<float2*>(sm) + g * GM::MP;
   const float2* __restrict__ chirp = a.chirp;
   const float2* __restrict__ H = a.H;
   const float csign = INV ? -1.f : 1.f;  // inverse uses conj(chirp)
@@ -89,12 +88,10 @@ __global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS) k_bluestein(BlueArgs 
     m = fmaf(xr, ci, xi * c.x);
   });
   auto sstore = [&](int i, float r, float m) {
-    sre[spad(i)] = r;
-    sim[spad(i)] = m;
+    sb[spad<S::SH>(i)] = make_float2(r, m);
   };
   auto sload = [&](int i, float& r, float& m) {
-    r = sre[spad(i)];
-    m = sim[spad(i)];
+    { const float2 v_ = sb[spad<S::SH>(i)]; r = v_.x; m = v_.y; }
   };
   if constexpr (S::P == 1) {
     // single-pass forward FFT: multiply by H in the store
@@ -106,7 +103,7 @@ __global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS) k_bluestein(BlueArgs 
   } else {
     pass_compute_store<LOGM, LE, 0, false>(j, vr, vi, sstore);
     __syncthreads();
-    smem_passes<LOGM, LE, false, 1, S::P - 1>(j, sre, sim);
+    smem_passes<LOGM, LE, false, 1, S::P - 1>(j, sb);
     pass_load<LOGM, LE, S::P - 1>(j, vr, vi, sload);
     __syncthreads();
     pass_compute_store<LOGM, LE, S::P - 1, false>(j, vr, vi, [&](int i, float r, float m) {
@@ -118,7 +115,7 @@ __global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS) k_bluestein(BlueArgs 
   __syncthreads();
 
   // ---- inverse m-point FFT (unscaled; 1/m is folded into H) + postmultiply
-  smem_passes<LOGM, LE, true, 0, S::P - 1>(j, sre, sim);
+  smem_passes<LOGM, LE, true, 0, S::P - 1>(j, sb);
   pass_load<LOGM, LE, S::P - 1>(j, vr, vi, sload);
   const float sc = INV ? 1.f / (float)n : 1.f;
   pass_compute_store<LOGM, LE, S::P - 1, true>(j, vr, vi, [&](int i, float r, float m) {

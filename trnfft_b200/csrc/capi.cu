@@ -15,6 +15,9 @@
 #include "../../include/trnfft_b200.h"
 #include "fft_common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
+
+#include <cstdlib>
 
 namespace tfb {
 
@@ -195,6 +198,21 @@ int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device) {
   return TRNFFT_SUCCESS;
 }
 
+int trnfft_device_status(int device, int* status, int clear) {
+  if (!status) return fail(TRNFFT_INVALID_VALUE, "device_status: null status pointer");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "device_status: cannot select device %d", device);
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_dev_status, sizeof(int));
+  if (e == cudaSuccess && clear && v) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(g_dev_status, &z, sizeof(int));
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "device_status");
+  *status = v;
+  return TRNFFT_SUCCESS;
+}
+
 int trnfft_plan_destroy(trnfft_plan_t plan) {
   if (!plan) return TRNFFT_SUCCESS;
   if (plan->chirp || plan->H) {
@@ -247,13 +265,23 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
     }
     case TRNFFT_ALG_STOCKHAM: {
       RowArgs a{in_re, in_im, out_re, out_im, batch, n, n, inverse ? (float)(1.0 / (double)n) : 1.0f};
-      e = launch_rows_c2c(plan->logn, inverse != 0, a, st);
+      // The bulk-copy (TMA) fed persistent kernel is opt-in
+      // (TRNFFT_B200_ROW_KERNEL=tma): on B200 the plain kernel measured faster
+      // because the row transform is bound by shared-memory instruction issue.
+      static const bool use_tma = [] {
+        const char* v = getenv("TRNFFT_B200_ROW_KERNEL");
+        return v && strcmp(v, "tma") == 0;
+      }();
+      if (use_tma && rows_c2c_tma_ok(plan->logn, a))
+        e = launch_rows_c2c_tma(plan->logn, inverse != 0, a, st);
+      else
+        e = launch_rows_c2c(plan->logn, inverse != 0, a, st);
       break;
     }
     case TRNFFT_ALG_BLUESTEIN: {
       if (!plan->H)
         return fail(TRNFFT_UNSUPPORTED, "exec_c2c: Bluestein length n=%lld (padded %lld) above the fused "
-                    "kernel's limit n <= 8193", (long long)n, (long long)plan->m);
+                    "kernel's limit n <= 8192", (long long)n, (long long)plan->m);
       BlueArgs a{in_re, in_im, out_re, out_im, batch, (int)n, plan->chirp, plan->H};
       e = launch_bluestein(plan->logm, 0, inverse != 0, a, st);
       break;

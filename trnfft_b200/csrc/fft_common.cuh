@@ -146,10 +146,14 @@ extern __device__ float2 g_tw[kTwN];
 
 __device__ __forceinline__ float2 tw_lookup(int idx) { return __ldg(&g_tw[idx]); }
 
-// Padded shared-memory index: one word of padding per 32 words breaks the
-// stride-R bank conflicts of the Stockham write pattern.
-__device__ __forceinline__ int spad(int i) { return i + (i >> 5); }
-__host__ __device__ constexpr int spad_size(int n) { return n + (n >> 5); }
+// Shared memory holds complex values interleaved (one float2 per element, so
+// one 8-byte access moves a value) with one float2 of padding after every
+// 2^SH elements.  With SH = log2 of the largest radix, the stride-R writes of
+// the first Stockham pass land in distinct bank pairs within each half-warp.
+template <int SH>
+__device__ __forceinline__ int spad(int i) { return i + (i >> SH); }
+template <int SH>
+__host__ __device__ constexpr int spad_size(int n) { return n + (n >> SH); }
 
 // ---------------------------------------------------------------------------
 // Stockham pass schedule for N = 2^LOGN with E = 2^LOGE values per thread.
@@ -162,6 +166,8 @@ struct Sched {
   static constexpr int E = 1 << LE;
   static constexpr int T = N / E;  // threads per transform
   static constexpr int P = (LOGN + LE - 1) / LE;
+  static constexpr int SH = LE;                    // shared-memory pad shift
+  static constexpr int NP = N + (N >> LE);         // padded float2 slots per transform
   static constexpr int logr(int p) {
     return (LOGN % LE == 0) ? LE : (p == 0 ? LOGN % LE : LE);
   }
@@ -245,25 +251,25 @@ __device__ __forceinline__ void pass_compute_store(int j, float (&vr)[Sched<LOGN
   }
 }
 
-// Run passes [P0, P1) entirely through shared memory (sre/sim padded, one
-// transform).  The caller has already placed the pass-P0 input in shared
-// memory and synchronised.  All threads of the block must call this.
+// Run passes [p, PEND) entirely through shared memory (`sb`: one transform,
+// padded float2 layout).  The caller has already placed the pass-p input in
+// shared memory and synchronised.  All threads of the block must call this.
 template <int LOGN, int LOGE, bool INV, int p, int PEND>
-__device__ __forceinline__ void smem_passes(int j, float* sre, float* sim) {
+__device__ __forceinline__ void smem_passes(int j, float2* sb) {
   if constexpr (p < PEND) {
     using S = Sched<LOGN, LOGE>;
     float vr[S::E], vi[S::E];
     pass_load<LOGN, LOGE, p>(j, vr, vi, [&](int i, float& a, float& b) {
-      a = sre[spad(i)];
-      b = sim[spad(i)];
+      const float2 v = sb[spad<S::SH>(i)];
+      a = v.x;
+      b = v.y;
     });
     __syncthreads();
     pass_compute_store<LOGN, LOGE, p, INV>(j, vr, vi, [&](int i, float a, float b) {
-      sre[spad(i)] = a;
-      sim[spad(i)] = b;
+      sb[spad<S::SH>(i)] = make_float2(a, b);
     });
     __syncthreads();
-    smem_passes<LOGN, LOGE, INV, p + 1, PEND>(j, sre, sim);
+    smem_passes<LOGN, LOGE, INV, p + 1, PEND>(j, sb);
   }
 }
 

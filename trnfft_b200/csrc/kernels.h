@@ -36,6 +36,8 @@ struct BlueArgs {
 cudaError_t launch_bluestein(int logm, int mode, bool inv, const BlueArgs& a, cudaStream_t st);
 
 cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st);
+bool rows_c2c_tma_ok(int logn, const RowArgs& a);
+cudaError_t launch_rows_c2c_tma(int logn, bool inv, const RowArgs& a, cudaStream_t st);
 cudaError_t launch_rows_r2c(int logm, const RowArgs& a, cudaStream_t st);
 cudaError_t launch_rows_c2r(int logm, const RowArgs& a, cudaStream_t st);
 

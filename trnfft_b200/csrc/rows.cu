@@ -15,6 +15,7 @@
 //          transform is returned)
 #include "fft_common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
 
 #include <cstdlib>
 
@@ -28,8 +29,8 @@ struct RowGeom {
   static_assert(S::T <= kRowThreads && kRowThreads % S::T == 0,
                 "one transform must fit in one block of kRowThreads threads");
   static constexpr int G = kRowThreads / S::T;  // transforms per block
-  static constexpr int NP = spad_size(S::N);
-  static constexpr size_t smem = (size_t)G * 2 * NP * sizeof(float);
+  static constexpr int NP = S::NP;
+  static constexpr size_t smem = (size_t)G * NP * sizeof(float2);
 };
 
 // ----------------------------------------------------------------------------
@@ -63,17 +64,14 @@ __global__ void __launch_bounds__(kRowThreads, MINB) k_c2c(RowArgs a) {
   if constexpr (S::P == 1) {
     pass_compute_store<LOGN, LOGE, 0, INV>(j, vr, vi, gstore);
   } else {
-    float* sre = sm + g * 2 * GM::NP;
-    float* sim = sre + GM::NP;
+    float2* sb = reinterpret_cast<float2*>(sm) + g * GM::NP;
     pass_compute_store<LOGN, LOGE, 0, INV>(j, vr, vi, [&](int i, float r, float m) {
-      sre[spad(i)] = r;
-      sim[spad(i)] = m;
+      sb[spad<S::SH>(i)] = make_float2(r, m);
     });
     __syncthreads();
-    smem_passes<LOGN, LOGE, INV, 1, S::P - 1>(j, sre, sim);
+    smem_passes<LOGN, LOGE, INV, 1, S::P - 1>(j, sb);
     pass_load<LOGN, LOGE, S::P - 1>(j, vr, vi, [&](int i, float& r, float& m) {
-      r = sre[spad(i)];
-      m = sim[spad(i)];
+      { const float2 v_ = sb[spad<S::SH>(i)]; r = v_.x; m = v_.y; }
     });
     pass_compute_store<LOGN, LOGE, S::P - 1, INV>(j, vr, vi, gstore);
   }
@@ -82,16 +80,15 @@ __global__ void __launch_bounds__(kRowThreads, MINB) k_c2c(RowArgs a) {
 // Runs the M-point forward FFT of the packed row through all passes and
 // leaves the result in shared memory.
 template <int LOGM, int LOGE, bool INV, class Ld>
-__device__ __forceinline__ void fft_to_smem(int j, float* sre, float* sim, Ld ld) {
+__device__ __forceinline__ void fft_to_smem(int j, float2* sb, Ld ld) {
   using S = Sched<LOGM, LOGE>;
   float vr[S::E], vi[S::E];
   pass_load<LOGM, LOGE, 0>(j, vr, vi, ld);
   pass_compute_store<LOGM, LOGE, 0, INV>(j, vr, vi, [&](int i, float r, float m) {
-    sre[spad(i)] = r;
-    sim[spad(i)] = m;
+    sb[spad<S::SH>(i)] = make_float2(r, m);
   });
   __syncthreads();
-  smem_passes<LOGM, LOGE, INV, 1, S::P>(j, sre, sim);
+  smem_passes<LOGM, LOGE, INV, 1, S::P>(j, sb);
 }
 
 // ----------------------------------------------------------------------------
@@ -111,10 +108,9 @@ __global__ void __launch_bounds__(kRowThreads) k_r2c(RowArgs a) {
   const float* __restrict__ x = a.xr + tt * a.in_stride;
   float* __restrict__ yr = a.yr + tt * a.out_stride;
   float* __restrict__ yi = a.yi + tt * a.out_stride;
-  float* sre = sm + g * 2 * GM::NP;
-  float* sim = sre + GM::NP;
+  float2* sb = reinterpret_cast<float2*>(sm) + g * GM::NP;
 
-  fft_to_smem<LOGM, LOGE, false>(j, sre, sim, [&](int i, float& r, float& m) {
+  fft_to_smem<LOGM, LOGE, false>(j, sb, [&](int i, float& r, float& m) {
     if (valid) {
       const float2 v = __ldg(reinterpret_cast<const float2*>(x) + i);
       r = v.x;
@@ -128,8 +124,8 @@ __global__ void __launch_bounds__(kRowThreads) k_r2c(RowArgs a) {
   for (int k = j; k <= M; k += S::T) {
     const int k0 = k & (M - 1);
     const int k1 = (M - k) & (M - 1);
-    const float zr = sre[spad(k0)], zi = sim[spad(k0)];
-    const float wr = sre[spad(k1)], wi = sim[spad(k1)];
+    const float2 z = sb[spad<S::SH>(k0)], w2 = sb[spad<S::SH>(k1)];
+    const float zr = z.x, zi = z.y, wr = w2.x, wi = w2.y;
     const float er = 0.5f * (zr + wr), ei = 0.5f * (zi - wi);
     const float orr = 0.5f * (zi + wi), oi = 0.5f * (wr - zr);
     const float2 w = tw_lookup(k << (kTwLog - LOGN));  // k <= M = N/2: index < table size
@@ -157,12 +153,11 @@ __global__ void __launch_bounds__(kRowThreads) k_c2r(RowArgs a) {
   const float* __restrict__ xr = a.xr + tt * a.in_stride;
   const float* __restrict__ xi = a.xi + tt * a.in_stride;
   float* __restrict__ y = a.yr + tt * a.out_stride;
-  float* sre = sm + g * 2 * GM::NP;
-  float* sim = sre + GM::NP;
+  float2* sb = reinterpret_cast<float2*>(sm) + g * GM::NP;
   const float sc = a.scale;  // 1/N
 
   // Z_k = E_k + i O_k with E_k = (X_k + conj X_{M-k})/2, O_k = (X_k - conj X_{M-k}) conj(W_N^k)/2
-  fft_to_smem<LOGM, LOGE, true>(j, sre, sim, [&](int k, float& r, float& m) {
+  fft_to_smem<LOGM, LOGE, true>(j, sb, [&](int k, float& r, float& m) {
     if (!valid) {
       r = 0.f;
       m = 0.f;
@@ -185,7 +180,10 @@ __global__ void __launch_bounds__(kRowThreads) k_c2r(RowArgs a) {
   // so multiplying by sc = 1/N yields z = (x[2n], x[2n+1]).
   if (valid) {
     float2* yo = reinterpret_cast<float2*>(y);
-    for (int n = j; n < M; n += S::T) yo[n] = make_float2(sre[spad(n)] * sc, sim[spad(n)] * sc);
+    for (int n = j; n < M; n += S::T) {
+      const float2 v = sb[spad<S::SH>(n)];
+      yo[n] = make_float2(v.x * sc, v.y * sc);
+    }
   }
 }
 
@@ -214,8 +212,16 @@ static cudaError_t launch_c2c_v(const RowArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// Measured defaults (B200, batch of 8M complex values, L2 flushed): radix-32
+// passes for N = 1024, three resident blocks per SM for N >= 2048.
+template <int LOGN>
+constexpr int default_row_variant() {
+  return LOGN == 10 ? 2 : (LOGN >= 11 ? 1 : 0);
+}
+
 template <int LOGN, bool INV>
 static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st, int variant) {
+  if (variant < 0) variant = default_row_variant<LOGN>();
   if constexpr (LOGN >= 8) {
     switch (variant) {
       case 1: return launch_c2c_v<LOGN, INV, RowVar<4, 3>>(a, st);
@@ -252,7 +258,7 @@ cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t s
   if (a.batch <= 0) return cudaSuccess;
   static const int variant = [] {
     const char* v = getenv("TRNFFT_B200_ROW_VARIANT");
-    return v ? atoi(v) : 0;
+    return v ? atoi(v) : -1;
   }();
 #define TFB_C2C_CASE(L) \
   case L: return inv ? launch_c2c_t<L, true>(a, st, variant) : launch_c2c_t<L, false>(a, st, variant);
@@ -285,6 +291,173 @@ cudaError_t launch_rows_c2r(int logm, const RowArgs& a, cudaStream_t st) {
     default: return cudaErrorInvalidValue;
   }
 #undef TFB_R_CASE
+}
+
+}  // namespace tfb
+
+// ============================================================================
+// Persistent, bulk-copy-fed variant of k_c2c.
+//
+// Each block loops over tiles of G consecutive transforms (G*N floats per
+// plane, contiguous in HBM).  One thread keeps STAGES tiles in flight with
+// 1-D bulk copies (cp.async.bulk, the TMA engine) into shared-memory stage
+// buffers; the block runs the Stockham passes of the current tile while the
+// next tiles stream in, so HBM reads never wait for the arithmetic.  The last
+// pass stores straight from registers to HBM (unit stride across threads).
+// ============================================================================
+namespace tfb {
+__device__ int g_dev_status;  // see tma.cuh
+}
+
+namespace tfb {
+
+template <int LOGN, int LOGE, int STAGES>
+struct TmaGeom {
+  using S = Sched<LOGN, LOGE>;
+  static constexpr int G = kRowThreads / S::T;
+  static constexpr int TILE = G * S::N;  // floats per plane per tile
+  static constexpr int NP = S::NP;
+  static constexpr size_t stage_bytes = (size_t)2 * TILE * sizeof(float);
+  static constexpr size_t xbytes = (size_t)G * NP * sizeof(float2);
+  static constexpr size_t bar_off = STAGES * stage_bytes + xbytes;
+  static constexpr size_t smem = bar_off + STAGES * sizeof(uint64_t);
+};
+
+template <int LOGN, int LOGE, bool INV, int STAGES>
+__global__ void __launch_bounds__(kRowThreads) k_c2c_tma(RowArgs a, long long ntiles) {
+  using S = Sched<LOGN, LOGE>;
+  using GM = TmaGeom<LOGN, LOGE, STAGES>;
+  static_assert(S::P >= 2, "bulk-copy variant needs at least two passes");
+  extern __shared__ __align__(128) unsigned char smraw[];
+  float* stages = reinterpret_cast<float*>(smraw);
+  float* xbase = reinterpret_cast<float*>(smraw + STAGES * GM::stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smraw + GM::bar_off);
+  const int tid = threadIdx.x;
+  const int g = tid / S::T;
+  const int j = tid % S::T;
+  float2* sb = reinterpret_cast<float2*>(xbase) + g * GM::NP;
+  const float sc = a.scale;
+
+  auto issue = [&](long long tile, int s) {
+    const long long row0 = tile * GM::G;
+    const long long rows = (a.batch - row0) < GM::G ? (a.batch - row0) : GM::G;
+    const uint32_t bytes = (uint32_t)(rows * S::N * sizeof(float));
+    float* dst = stages + (size_t)s * 2 * GM::TILE;
+    mbar_arrive_expect_tx(&bars[s], 2 * bytes);
+    bulk_g2s(dst, a.xr + row0 * S::N, bytes, &bars[s]);
+    bulk_g2s(dst + GM::TILE, a.xi + row0 * S::N, bytes, &bars[s]);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  long long issued = 0;  // meaningful in thread 0 only
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      const long long tile = blockIdx.x + (long long)s * gridDim.x;
+      if (tile < ntiles) {
+        issue(tile, s);
+        ++issued;
+      }
+    }
+  }
+
+  long long it = 0;
+  for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+    const int s = (int)(it % STAGES);
+    const uint32_t parity = (uint32_t)((it / STAGES) & 1);
+    const bool ok = __syncthreads_and(mbar_wait_bounded(&bars[s], parity));
+    if (!ok) {
+      if (tid == 0) atomicExch(&g_dev_status, kStatusWaitTimeout);
+      break;
+    }
+    const long long t = tile * GM::G + g;
+    const bool valid = t < a.batch;
+    const float* str = stages + (size_t)s * 2 * GM::TILE + g * S::N;
+    const float* sti = str + GM::TILE;
+    float vr[S::E], vi[S::E];
+    pass_load<LOGN, LOGE, 0>(j, vr, vi, [&](int i, float& r, float& m) {
+      r = str[i];
+      m = sti[i];
+    });
+    __syncthreads();  // stage s fully read by every thread
+    if (tid == 0) {
+      const long long next = tile + (long long)STAGES * gridDim.x;
+      if (next < ntiles) {
+        fence_proxy_async();
+        issue(next, s);
+        ++issued;
+      }
+    }
+    pass_compute_store<LOGN, LOGE, 0, INV>(j, vr, vi, [&](int i, float r, float m) {
+      sb[spad<S::SH>(i)] = make_float2(r, m);
+    });
+    __syncthreads();
+    smem_passes<LOGN, LOGE, INV, 1, S::P - 1>(j, sb);
+    pass_load<LOGN, LOGE, S::P - 1>(j, vr, vi, [&](int i, float& r, float& m) {
+      { const float2 v_ = sb[spad<S::SH>(i)]; r = v_.x; m = v_.y; }
+    });
+    float* yr = a.yr + (valid ? t : 0) * a.out_stride;
+    float* yi = a.yi + (valid ? t : 0) * a.out_stride;
+    pass_compute_store<LOGN, LOGE, S::P - 1, INV>(j, vr, vi, [&](int i, float r, float m) {
+      if (valid) {
+        yr[i] = r * sc;
+        yi[i] = m * sc;
+      }
+    });
+  }
+  // After a timeout, drain (bounded) every copy this block still has in flight
+  // before its shared memory is released.
+  if (tid == 0) {
+    for (long long k = it; k < issued; ++k)
+      (void)mbar_wait_bounded(&bars[k % STAGES], (uint32_t)((k / STAGES) & 1));
+  }
+}
+
+template <int LOGN, bool INV, int LOGE, int STAGES>
+static cudaError_t launch_c2c_tma_v(const RowArgs& a, cudaStream_t st) {
+  using GM = TmaGeom<LOGN, LOGE, STAGES>;
+  auto kern = k_c2c_tma<LOGN, LOGE, INV, STAGES>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0, per_sm = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowThreads, GM::smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  const long long ntiles = (a.batch + GM::G - 1) / GM::G;
+  long long grid = (long long)sms * per_sm;
+  if (grid > ntiles) grid = ntiles;
+  kern<<<(unsigned)grid, kRowThreads, GM::smem, st>>>(a, ntiles);
+  return cudaGetLastError();
+}
+
+bool rows_c2c_tma_ok(int logn, const RowArgs& a) {
+  // 16-byte aligned planes with contiguous rows, two or more passes
+  const bool al = ((reinterpret_cast<uintptr_t>(a.xr) | reinterpret_cast<uintptr_t>(a.xi)) & 15) == 0;
+  return al && logn >= 6 && logn <= 12 && a.in_stride == (1LL << logn);
+}
+
+cudaError_t launch_rows_c2c_tma(int logn, bool inv, const RowArgs& a, cudaStream_t st) {
+  if (a.batch <= 0) return cudaSuccess;
+  static const int stages = [] {
+    const char* v = getenv("TRNFFT_B200_TMA_STAGES");
+    return (v && atoi(v) == 3) ? 3 : 2;
+  }();
+#define TFB_TMA_CASE(L)                                                                      \
+  case L:                                                                                    \
+    if (stages == 3)                                                                         \
+      return inv ? launch_c2c_tma_v<L, true, 4, 3>(a, st) : launch_c2c_tma_v<L, false, 4, 3>(a, st); \
+    return inv ? launch_c2c_tma_v<L, true, 4, 2>(a, st) : launch_c2c_tma_v<L, false, 4, 2>(a, st);
+  switch (logn) {
+    TFB_TMA_CASE(6) TFB_TMA_CASE(7) TFB_TMA_CASE(8) TFB_TMA_CASE(9)
+    TFB_TMA_CASE(10) TFB_TMA_CASE(11) TFB_TMA_CASE(12)
+    default: return cudaErrorInvalidValue;
+  }
+#undef TFB_TMA_CASE
 }
 
 }  // namespace tfb
