@@ -86,8 +86,8 @@ TRNFFT_API int trnfft_device_status(int device, int* status, int clear);
 TRNFFT_API int trnfft_plan_destroy(trnfft_plan_t plan);
 
 /* Plan properties: algorithm (trnfft_algorithm), padded length (Bluestein m,
- * else n) and the work-area bytes that trnfft_exec_c2c needs for `batch`
- * transforms (0 when none). Replaces FFTPlan's fields (trnfft/plan.py:19-28). */
+ * else n) and the work-area bytes that an IN-PLACE trnfft_exec_c2c needs for
+ * `batch` transforms (0 when none; out-of-place calls never need one). Replaces FFTPlan's fields (trnfft/plan.py:19-28). */
 TRNFFT_API int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* padded_n, int64_t batch,
                       int64_t* work_bytes);
 
@@ -95,10 +95,24 @@ TRNFFT_API int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* pa
  * Replaces fft_core(x, inverse) (trnfft/fft_core.py:22-50) -> _cooley_tukey
  * (fft_core.py:53-117) / _bluestein (fft_core.py:1285-1376), reached from
  * trnfft.fft / trnfft.ifft (trnfft/api.py:22-35).
- * `work` is a device buffer of trnfft_plan_query's work_bytes (may be NULL
- * when that is 0).  In-place (in == out) is allowed. */
+ * Power-of-two n > 4096 (up to 2^30) run as two or three column-tile passes
+ * (four-step / six-step, trnfft/nki/multicore.py:151-219).  In-place calls
+ * (in == out) are allowed; for n > 4096 they need `work`, a device buffer
+ * of trnfft_plan_query's work_bytes; out-of-place calls need none (NULL). */
 TRNFFT_API int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out_re,
                     float* out_im, int64_t batch, int inverse, void* work, void* stream);
+
+/* Transforms along the middle axis of a contiguous [outer][n][inner] array
+ * (element (o, j, s) at o*n*inner + j*inner + s), for power-of-two n up to
+ * 2^20 (inner == 1 is exactly trnfft_exec_c2c).  Replaces the per-axis
+ * transpose + contiguous copy + fft_core + transpose back of
+ * _fft_along_dim (trnfft/api.py:496-516) used by fft2/fftn/ifftn
+ * (trnfft/api.py:105-167): the column tiles are read in place.
+ * An in-place call with n > 1024 needs `work` of plan_query's size for
+ * batch = outer*inner. */
+TRNFFT_API int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, const float* in_im,
+                                    float* out_re, float* out_im, int64_t outer, int64_t inner,
+                                    int inverse, void* work, void* stream);
 
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex

@@ -1,0 +1,139 @@
+"""GPU parity of the large power-of-two (multi-pass) transforms, the strided-axis
+transforms behind fft2/fftn, and the four-step single transform."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import trnfft_b200 as trnfft
+from trnfft_b200 import ComplexTensor, _lib
+from trnfft_b200.nki import multicore
+from oracle import trnfft_oracle as O
+from tests.helpers import TOL, cplx, cuda, host, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("n", [8192, 16384])
+def test_vs_reference_golden(golden, n):
+    g = golden("pow2_large")
+    y = trnfft.fft(ComplexTensor(cuda(g[f"x_re_{n}"]), cuda(g[f"x_im_{n}"])))
+    assert rel_l2(cplx(y), g[f"fft_re_{n}"] + 1j * g[f"fft_im_{n}"]) < TOL
+
+
+@pytest.mark.parametrize("logn", [13, 14, 16, 18, 20, 21, 22])
+def test_vs_fp64(logn):
+    n = 1 << logn
+    b = max(1, (1 << 22) // n)
+    rng = np.random.default_rng(logn)
+    x = (rng.standard_normal((b, n)) + 1j * rng.standard_normal((b, n))).astype(np.complex64)
+    X = trnfft.fft(ComplexTensor(cuda(x.real), cuda(x.imag)))
+    assert rel_l2(cplx(X), np.fft.fft(x.astype(np.complex128))) < 2e-6
+    Z = trnfft.ifft(ComplexTensor(cuda(x.real), cuda(x.imag)))
+    assert rel_l2(cplx(Z), np.fft.ifft(x.astype(np.complex128))) < 2e-6
+
+
+@pytest.mark.parametrize("n", [4096, 65536])
+def test_four_step_vs_reference_golden(golden, n):
+    g = golden("four_step")
+    x = ComplexTensor(cuda(g[f"x_re_{n}"]), cuda(g[f"x_im_{n}"]))
+    multicore.set_multicore(True)
+    try:
+        y = multicore.multi_core_fft(x)
+        z = multicore.multi_core_fft(x, inverse=True)
+    finally:
+        multicore.set_multicore(False)
+    assert rel_l2(cplx(y), g[f"sp_re_{n}"] + 1j * g[f"sp_im_{n}"]) < TOL
+    assert rel_l2(cplx(z), g[f"spi_re_{n}"] + 1j * g[f"spi_im_{n}"]) < TOL
+
+
+def test_in_place_with_work_area():
+    n = 1 << 15
+    b = 3
+    torch.manual_seed(0)
+    xr = torch.randn(b, n, device="cuda")
+    xi = torch.randn(b, n, device="cuda")
+    ref = torch.fft.fft(torch.complex(xr, xi).to(torch.complex128))
+    plan = _lib.device_plan(n, xr.device)
+    wb = plan.work_bytes(b)
+    assert wb == 8 * n * b
+    work = torch.empty(wb, dtype=torch.uint8, device="cuda")
+    _lib.call("trnfft_exec_c2c", plan.handle, _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(xr), _lib.ptr(xi), b, 0,
+              _lib.ptr(work), _lib.stream_ptr(xr.device))
+    got = host(xr) + 1j * host(xi)
+    assert rel_l2(got, ref.cpu().numpy()) < 2e-6
+    with pytest.raises(ValueError, match="work area"):
+        _lib.call("trnfft_exec_c2c", plan.handle, _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(xr), _lib.ptr(xi), b, 0,
+                  None, _lib.stream_ptr(xr.device))
+
+
+def test_full_size_2_30_roundtrip_and_parseval():
+    """Config 5 size (N = 2^30, 8 GiB planar): size-independent properties --
+    ifft(fft(x)) == x, Parseval, and the DC bin equals the sum."""
+    n = 1 << 30
+    g = torch.Generator(device="cuda").manual_seed(5)
+    xr = torch.randn(n, device="cuda", generator=g)
+    xi = torch.randn(n, device="cuda", generator=g)
+    X = trnfft.fft(ComplexTensor(xr, xi))
+    dc = complex(xr.double().sum().item(), xi.double().sum().item())
+    assert abs(complex(X.real[0].item(), X.imag[0].item()) - dc) < 1e-3 * np.sqrt(n)
+    ex = (xr.double() ** 2).sum() + (xi.double() ** 2).sum()
+    eX = ((X.real.double() ** 2).sum() + (X.imag.double() ** 2).sum()) / n
+    assert abs(float(eX / ex) - 1.0) < 1e-5
+    back = trnfft.ifft(X)
+    del X
+    err = torch.sqrt(((back.real - xr).double() ** 2).sum() + ((back.imag - xi).double() ** 2).sum())
+    assert float(err / torch.sqrt(ex)) < 2e-6
+
+
+def test_fft2_vs_reference_golden(golden):
+    g = golden("nd")
+    for key in ["16x32", "64x64", "8x256"]:
+        x = ComplexTensor(cuda(g[f"x_re_{key}"]), cuda(g[f"x_im_{key}"]))
+        assert rel_l2(cplx(trnfft.fft2(x)), g[f"fft2_re_{key}"] + 1j * g[f"fft2_im_{key}"]) < TOL
+        z = trnfft.ifftn(x, dim=(-2, -1))
+        assert rel_l2(cplx(z), g[f"ifft2_re_{key}"] + 1j * g[f"ifft2_im_{key}"]) < TOL
+    x3 = cuda(g["x3"])
+    assert rel_l2(cplx(trnfft.fftn(x3)), g["fftn3_re"] + 1j * g["fftn3_im"]) < TOL
+    assert rel_l2(cplx(trnfft.fftn(x3, dim=(0, 2))), g["fftn3_d02_re"] + 1j * g["fftn3_d02_im"]) < TOL
+    r = trnfft.rfftn(x3)
+    assert rel_l2(cplx(r), g["rfftn3_re"] + 1j * g["rfftn3_im"]) < TOL
+    assert rel_l2(host(trnfft.irfftn(r, s=x3.shape)), g["irfftn3"]) < TOL
+    r2 = trnfft.rfft2(cuda(g["x2"]), s=(16, 32))
+    assert rel_l2(cplx(r2), g["rfft2_s_re"] + 1j * g["rfft2_s_im"]) < TOL
+    xh = ComplexTensor(cuda(g["h_re"]), cuda(g["h_im"]))
+    assert rel_l2(host(trnfft.hfft(xh, n=16)), g["hfft_16"]) < TOL
+    ih = trnfft.ihfft(cuda(g["ih_x"]))
+    assert rel_l2(cplx(ih), g["ihfft_re"] + 1j * g["ihfft_im"]) < TOL
+
+
+@pytest.mark.parametrize("shape,dim", [((3, 1024, 40), 1), ((2, 4096, 24), 1), ((5, 7, 9), 1),
+                                       ((64, 2048), 0), ((1 << 13, 16), 0), ((6, 12, 64), 0)])
+def test_axis_vs_fp64(shape, dim):
+    rng = np.random.default_rng(sum(shape))
+    x = (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)).astype(np.complex64)
+    y = trnfft.fftn(ComplexTensor(cuda(x.real), cuda(x.imag)), dim=(dim,))
+    assert rel_l2(cplx(y), np.fft.fft(x.astype(np.complex128), axis=dim)) < 2e-6
+
+
+def test_fft2_large_vs_fp64():
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((1024, 2048)) + 1j * rng.standard_normal((1024, 2048))).astype(np.complex64)
+    y = trnfft.fft2(ComplexTensor(cuda(x.real), cuda(x.imag)))
+    assert rel_l2(cplx(y), np.fft.fft2(x.astype(np.complex128))) < 2e-6
+
+
+def test_axis_autograd_matches_torch():
+    torch.manual_seed(2)
+    xr = torch.randn(4, 32, 16, device="cuda", requires_grad=True)
+    xi = torch.randn(4, 32, 16, device="cuda", requires_grad=True)
+    y = trnfft.fft2(ComplexTensor(xr, xi))
+    (y.real * 3 + y.imag ** 2).sum().backward()
+    zr = xr.detach().clone().requires_grad_(True)
+    zi = xi.detach().clone().requires_grad_(True)
+    z = torch.fft.fft2(torch.complex(zr, zi))
+    (z.real * 3 + z.imag ** 2).sum().backward()
+    assert rel_l2(host(xr.grad), host(zr.grad)) < 1e-5
+    assert rel_l2(host(xi.grad), host(zi.grad)) < 1e-5

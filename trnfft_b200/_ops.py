@@ -47,11 +47,57 @@ def c2c_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool) -> tuple[torch.Te
     batch = a.shape[0]
     if batch and n:
         plan = _lib.device_plan(n, a.device)
-        wb = plan.work_bytes(batch)
-        work = torch.empty(wb, dtype=torch.uint8, device=a.device) if wb else None
+        # out of place: no work area is needed
         _lib.call("trnfft_exec_c2c", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi),
-                  batch, int(bool(inverse)), _lib.ptr(work), _lib.stream_ptr(a.device))
+                  batch, int(bool(inverse)), None, _lib.stream_ptr(a.device))
     return yr.reshape(shape), yi.reshape(shape)
+
+
+def axis_supported(n: int) -> bool:
+    """Power-of-two lengths the strided-axis kernels handle (up to 2^20)."""
+    return n >= 1 and (n & (n - 1)) == 0 and n <= (1 << 20)
+
+
+def c2c_axis_raw(xr: torch.Tensor, xi: torch.Tensor, dim: int, inverse: bool):
+    """Transform along axis `dim` of contiguous tensors without moving it last."""
+    _check(xr, "real part")
+    _check(xi, "imaginary part")
+    shape = xr.shape
+    n = shape[dim]
+    outer = 1
+    for s_ in shape[:dim]:
+        outer *= s_
+    inner = 1
+    for s_ in shape[dim + 1:]:
+        inner *= s_
+    a = xr.contiguous()
+    b = xi.contiguous()
+    yr = torch.empty_like(a)
+    yi = torch.empty_like(b)
+    if a.numel():
+        plan = _lib.device_plan(n, a.device)
+        _lib.call("trnfft_exec_c2c_axis", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi),
+                  outer, inner, int(bool(inverse)), None, _lib.stream_ptr(a.device))
+    return yr, yi
+
+
+class _C2CAxis(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xr, xi, dim: int, inverse: bool):
+        ctx.dim, ctx.inverse, ctx.n = dim, inverse, xr.shape[dim]
+        return c2c_axis_raw(xr, xi, dim, inverse)
+
+    @staticmethod
+    def backward(ctx, gr, gi):
+        dr, di = c2c_axis_raw(gr.contiguous(), gi.contiguous(), ctx.dim, not ctx.inverse)
+        s = (1.0 / ctx.n) if ctx.inverse else float(ctx.n)
+        return dr * s, di * s, None, None
+
+
+def c2c_axis(xr, xi, dim: int, inverse: bool):
+    if torch.is_grad_enabled() and (xr.requires_grad or xi.requires_grad):
+        return _C2CAxis.apply(xr, xi, dim, inverse)
+    return c2c_axis_raw(xr, xi, dim, inverse)
 
 
 def _r2c_native(n: int) -> bool:

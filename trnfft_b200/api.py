@@ -255,11 +255,20 @@ def _resize_last(x: ComplexTensor, n: int) -> ComplexTensor:
 
 
 def _fft_along_dim(x: ComplexTensor, dim: int, inverse: bool) -> ComplexTensor:
-    """1-D transform along one dimension of an N-D tensor."""
+    """1-D transform along one dimension of an N-D tensor.
+
+    Power-of-two lengths run the strided-axis kernel in place of the
+    reference's transpose/copy/transform/transpose (trnfft/api.py:496-516).
+    """
     ndim = len(x.shape)
     dim = dim % ndim
     if dim == ndim - 1:
         return fft_core(x, inverse=inverse)
+    n = x.shape[dim]
+    if n > 1 and _ops.axis_supported(n):
+        (xr, xi), restore = place(x.real, x.imag)
+        yr, yi = _ops.c2c_axis(xr, xi, dim, bool(inverse))
+        return ComplexTensor(restore(yr), restore(yi))
     xr = x.real.movedim(dim, -1)
     xi = x.imag.movedim(dim, -1)
     y = fft_core(ComplexTensor(xr, xi), inverse=inverse)

@@ -118,7 +118,130 @@ struct trnfft_plan_s {
   int logm = -1;
   float2* chirp = nullptr;  // Bluestein: n entries
   float2* H = nullptr;      // Bluestein: m entries
+  float2* tw_hi = nullptr;  // power of two n > 1024: W_n^(i << tw_split)
+  float2* tw_lo = nullptr;  // power of two n > 1024: W_n^i, i < 2^tw_split
+  int tw_split = 0;
 };
+
+// Two-level twiddle tables for W_n, n = 2^logn: W_n^e = hi[e >> s] * lo[e & (2^s - 1)].
+static int make_twiddle_tables(trnfft_plan_s* p) {
+  const int L = p->logn;
+  const int sp = (L + 1) / 2;
+  const int64_t nlo = int64_t(1) << sp, nhi = int64_t(1) << (L - sp);
+  std::vector<float2> lo(nlo), hi(nhi);
+  const double n = std::ldexp(1.0, L);
+  for (int64_t i = 0; i < nlo; ++i) {
+    const double a = -2.0 * M_PI * (double)i / n;
+    lo[i] = make_float2((float)std::cos(a), (float)std::sin(a));
+  }
+  for (int64_t i = 0; i < nhi; ++i) {
+    const double a = -2.0 * M_PI * (double)(i << sp) / n;
+    hi[i] = make_float2((float)std::cos(a), (float)std::sin(a));
+  }
+  cudaError_t e = cudaMalloc(&p->tw_lo, sizeof(float2) * nlo);
+  if (e == cudaSuccess) e = cudaMalloc(&p->tw_hi, sizeof(float2) * nhi);
+  if (e != cudaSuccess) return fail(TRNFFT_ALLOC_FAILED, "plan_create: %s", cudaGetErrorString(e));
+  e = cudaMemcpy(p->tw_lo, lo.data(), sizeof(float2) * nlo, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(p->tw_hi, hi.data(), sizeof(float2) * nhi, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "plan_create: uploading twiddle tables");
+  p->tw_split = sp;
+  return TRNFFT_SUCCESS;
+}
+
+static ColArgs col_base(const trnfft_plan_s* p) {
+  ColArgs c;
+  std::memset(&c, 0, sizeof c);
+  c.O1 = 1;
+  c.O2 = 1;
+  c.scale = 1.f;
+  c.nmask = p->n - 1;
+  c.tw_split = p->tw_split;
+  c.tw_hi = p->tw_hi;
+  c.tw_lo = p->tw_lo;
+  c.tw_mul = 1;
+  return c;
+}
+
+static constexpr int kMaxColLog = 10;  // column passes transform up to 1024 points on chip
+static constexpr int kMaxMultipassLog = 30;
+
+// Contiguous rows of n = 2^p > 4096 points, out of place (in != out):
+// p <= 20: n = N1*N3 (n = n1 + N1*n3, k = k3 + N3*k1), two passes;
+// p <= 30: n = N1*N2*N3 (n = n1 + N1*n2 + N1*N2*n3, k = k3 + N3*k2 + N3*N2*k1), three passes.
+static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr,
+                                      float* yi, int64_t batch, bool inv, cudaStream_t st) {
+  const int L = p->logn;
+  const long long N = p->n;
+  const float sc = inv ? (float)(1.0 / (double)N) : 1.f;
+  cudaError_t e;
+  if (L <= 2 * kMaxColLog) {
+    const int l1 = L / 2, l3 = L - l1;
+    const long long N1 = 1LL << l1, N3 = 1LL << l3;
+    ColArgs a = col_base(p);  // FFT over n3, columns n1, rows n1*N3 + k3, twiddle W_N^{n1*k3}
+    a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
+    a.ncols = N1; a.O2 = batch; a.is_o2 = N; a.is_j = N1;
+    a.os_o2 = N; a.os_c = N3;
+    a.has_tw = 1; a.tw_c = 1;
+    e = launch_colpass(l3, inv, 1, a, st);
+    if (e != cudaSuccess) return e;
+    ColArgs b = col_base(p);  // FFT over n1 in place, columns k3
+    b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
+    b.ncols = N3; b.O2 = batch; b.is_o2 = N; b.is_j = N3;
+    b.os_o2 = N; b.os_k = N3; b.scale = sc;
+    return launch_colpass(l1, inv, 0, b, st);
+  }
+  const int l1 = L / 3, l2 = (L - l1) / 2, l3 = L - l1 - l2;
+  const long long N1 = 1LL << l1, N2 = 1LL << l2, N3 = 1LL << l3;
+  ColArgs a = col_base(p);  // FFT over n3; columns n1, outer n2; rows (n1*N2 + n2)*N3 + k3
+  a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
+  a.ncols = N1; a.O1 = N2; a.O2 = batch; a.is_o1 = N1; a.is_o2 = N; a.is_j = N1 * N2;
+  a.os_o1 = N3; a.os_o2 = N; a.os_c = N2 * N3;
+  a.has_tw = 1; a.tw_mul = N1; a.tw_b = 1;  // W_{N2 N3}^{n2 k3} = W_N^{N1 n2 k3}
+  e = launch_colpass(l3, inv, 1, a, st);
+  if (e != cudaSuccess) return e;
+  ColArgs b = col_base(p);  // FFT over n2 in place; columns k3, outer n1; twiddle W_N^{n1 (k3 + N3 k2)}
+  b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
+  b.ncols = N3; b.O1 = N1; b.O2 = batch; b.is_o1 = N2 * N3; b.is_o2 = N; b.is_j = N3;
+  b.os_o1 = N2 * N3; b.os_o2 = N; b.os_k = N3;
+  b.has_tw = 1; b.tw_a = 1; b.tw_b = N3;
+  e = launch_colpass(l2, inv, 0, b, st);
+  if (e != cudaSuccess) return e;
+  ColArgs c = col_base(p);  // FFT over n1 in place; columns (k2, k3)
+  c.xr = yr; c.xi = yi; c.yr = yr; c.yi = yi;
+  c.ncols = N2 * N3; c.O2 = batch; c.is_o2 = N; c.is_j = N2 * N3;
+  c.os_o2 = N; c.os_k = N2 * N3; c.scale = sc;
+  return launch_colpass(l1, inv, 0, c, st);
+}
+
+// Transforms along the middle axis of an [outer][n][inner] array, inner > 1.
+static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr, float* yi,
+                            int64_t outer, int64_t inner, bool inv, cudaStream_t st) {
+  const int L = p->logn;
+  const long long n = p->n;
+  const float sc = inv ? (float)(1.0 / (double)n) : 1.f;
+  if (L <= kMaxColLog) {
+    ColArgs a = col_base(p);
+    a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
+    a.ncols = inner; a.O2 = outer; a.is_o2 = n * inner; a.is_j = inner;
+    a.os_o2 = n * inner; a.os_k = inner; a.scale = sc;
+    return launch_colpass(L, inv, 0, a, st);
+  }
+  // n = L1*L2, point n1 + L1*n2, output k2 + L2*k1 (out of place first pass)
+  const int l1 = L / 2, l2 = L - l1;
+  const long long L1 = 1LL << l1, L2 = 1LL << l2;
+  ColArgs a = col_base(p);  // FFT over n2; outer n1; output (n1*L2 + k2)*S + s; twiddle W_n^{n1 k2}
+  a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
+  a.ncols = inner; a.O1 = L1; a.O2 = outer; a.is_o1 = inner; a.is_o2 = n * inner; a.is_j = L1 * inner;
+  a.os_o1 = L2 * inner; a.os_o2 = n * inner; a.os_k = inner;
+  a.has_tw = 1; a.tw_b = 1;
+  cudaError_t e = launch_colpass(l2, inv, 0, a, st);
+  if (e != cudaSuccess) return e;
+  ColArgs b = col_base(p);  // FFT over n1 in place; outer k2
+  b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
+  b.ncols = inner; b.O1 = L2; b.O2 = outer; b.is_o1 = inner; b.is_o2 = n * inner; b.is_j = L2 * inner;
+  b.os_o1 = inner; b.os_o2 = n * inner; b.os_k = L2 * inner; b.scale = sc;
+  return launch_colpass(l1, inv, 0, b, st);
+}
 
 // Bluestein tables: chirp_k = exp(-i*pi*(k^2 mod 2n)/n) (exact integer
 // reduction of the angle, then double trig) and H = FFT_m(h)/m with
@@ -194,6 +317,13 @@ int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device) {
       }
     }
   }
+  if (p->logn > kMaxColLog && p->logn <= kMaxMultipassLog) {
+    int rc3 = make_twiddle_tables(p);
+    if (rc3) {
+      trnfft_plan_destroy(p);
+      return rc3;
+    }
+  }
   *plan = p;
   return TRNFFT_SUCCESS;
 }
@@ -220,6 +350,11 @@ int trnfft_plan_destroy(trnfft_plan_t plan) {
     if (plan->chirp) cudaFree(plan->chirp);
     if (plan->H) cudaFree(plan->H);
   }
+  if (plan->tw_hi || plan->tw_lo) {
+    DeviceGuard g(plan->device);
+    if (plan->tw_hi) cudaFree(plan->tw_hi);
+    if (plan->tw_lo) cudaFree(plan->tw_lo);
+  }
   delete plan;
   return TRNFFT_SUCCESS;
 }
@@ -229,8 +364,9 @@ int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* padded_n, int
   if (!plan) return fail(TRNFFT_INVALID_VALUE, "plan_query: null plan");
   if (algorithm) *algorithm = plan->algorithm;
   if (padded_n) *padded_n = plan->algorithm == TRNFFT_ALG_BLUESTEIN ? plan->m : plan->n;
-  if (work_bytes) *work_bytes = 0;
-  (void)batch;
+  // Only an in-place multi-pass transform needs a work area (a copy of the input).
+  if (work_bytes)
+    *work_bytes = plan->algorithm == TRNFFT_ALG_MULTIPASS ? (int64_t)(2 * sizeof(float)) * plan->n * batch : 0;
   return TRNFFT_SUCCESS;
 }
 
@@ -278,6 +414,25 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
         e = launch_rows_c2c(plan->logn, inverse != 0, a, st);
       break;
     }
+    case TRNFFT_ALG_MULTIPASS: {
+      if (plan->logn > kMaxMultipassLog)
+        return fail(TRNFFT_UNSUPPORTED, "exec_c2c: n=2^%d above the supported 2^%d", plan->logn, kMaxMultipassLog);
+      const float* xr = in_re;
+      const float* xi = in_im;
+      if (in_re == out_re || in_im == out_im) {
+        // the first pass scatters rows, so an in-place call copies the input aside
+        if (!work) return fail(TRNFFT_INVALID_VALUE, "exec_c2c: in-place n=%lld needs the work area", (long long)n);
+        float* w = static_cast<float*>(work);
+        const size_t bytes = sizeof(float) * (size_t)n * (size_t)batch;
+        e = cudaMemcpyAsync(w, in_re, bytes, cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(w + (size_t)n * batch, in_im, bytes, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) break;
+        xr = w;
+        xi = w + (size_t)n * batch;
+      }
+      e = run_rows_multipass(plan, xr, xi, out_re, out_im, batch, inverse != 0, st);
+      break;
+    }
     case TRNFFT_ALG_BLUESTEIN: {
       if (!plan->H)
         return fail(TRNFFT_UNSUPPORTED, "exec_c2c: Bluestein length n=%lld (padded %lld) above the fused "
@@ -290,6 +445,39 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
       return fail(TRNFFT_UNSUPPORTED, "exec_c2c: n=%lld not supported yet", (long long)n);
   }
   if (e != cudaSuccess) return cuda_fail(e, "exec_c2c");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out_re,
+                         float* out_im, int64_t outer, int64_t inner, int inverse, void* work, void* stream) {
+  if (!plan) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis: null plan");
+  if (outer < 0 || inner < 1) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis: bad outer/inner");
+  if (outer == 0) return TRNFFT_SUCCESS;
+  if (inner == 1) return trnfft_exec_c2c(plan, in_re, in_im, out_re, out_im, outer, inverse, work, stream);
+  int rc = check_ptrs("exec_c2c_axis", {in_re, in_im, out_re, out_im}, 4);
+  if (rc) return rc;
+  if (plan->algorithm == TRNFFT_ALG_COPY) {
+    return trnfft_exec_c2c(plan, in_re, in_im, out_re, out_im, outer * inner, inverse, work, stream);
+  }
+  if (plan->logn < 1 || plan->logn > 2 * kMaxColLog)
+    return fail(TRNFFT_UNSUPPORTED, "exec_c2c_axis: n=%lld (power of two up to 2^20 only)", (long long)plan->n);
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_c2c_axis: cannot select device %d", plan->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float* xr = in_re;
+  const float* xi = in_im;
+  cudaError_t e = cudaSuccess;
+  if (plan->logn > kMaxColLog && (in_re == out_re || in_im == out_im)) {
+    if (!work) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis: in-place n=%lld needs the work area", (long long)plan->n);
+    float* w = static_cast<float*>(work);
+    const size_t cnt = (size_t)plan->n * outer * inner;
+    e = cudaMemcpyAsync(w, in_re, cnt * sizeof(float), cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(w + cnt, in_im, cnt * sizeof(float), cudaMemcpyDeviceToDevice, st);
+    xr = w;
+    xi = w + cnt;
+  }
+  if (e == cudaSuccess) e = run_axis(plan, xr, xi, out_re, out_im, outer, inner, inverse != 0, st);
+  if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_axis");
   return TRNFFT_SUCCESS;
 }
 

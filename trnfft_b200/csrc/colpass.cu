@@ -1,0 +1,145 @@
+// Column-tile FFT pass: the building block of the multi-pass large-N
+// transforms and of transforms along a strided axis (fft2 / fftn).
+//
+// A tile is CT neighbouring "columns" (unit stride in HBM) of L-point
+// transforms whose points are `is_j` floats apart.  The block loads the tile
+// with coalesced reads (CT consecutive floats per point), keeps each column
+// as one padded float2 transform in shared memory, runs every Stockham pass
+// of the L-point FFT on chip, applies an optional twiddle W_N^e, and stores
+// the tile either column-wise again (KIND 0, in place allowed) or row-wise
+// (KIND 1: column c becomes a contiguous run of L outputs, which is the
+// transposition step of the four-step / six-step algorithm).
+//
+// Four-step reference: trnfft/nki/multicore.py:151-219 (column DFTs, twiddle
+// exp(sign*2*pi*i*l*k1/N), row DFTs, column-major flatten), which runs the
+// twiddle on the host and materialises two transposes.  Here the twiddle is
+// fused into the pass that produces its operand and the transposes are the
+// store pattern of the first pass.
+#include "fft_common.cuh"
+#include "kernels.h"
+
+namespace tfb {
+
+template <int LOGL>
+struct ColGeom {
+  static constexpr int LE = 4;
+  using S = Sched<LOGL, LE>;
+  static constexpr int L = S::N;
+  static constexpr int CT0 = 256 / S::T;
+  static constexpr int CT = CT0 < 8 ? 8 : (CT0 > 64 ? 64 : CT0);
+  static constexpr int THREADS = CT * S::T;
+  // column pitch in float2: CT columns of one half-warp land in distinct banks
+  static constexpr int R16 = CT >= 16 ? 1 : 16 / CT;
+  static constexpr int PITCH = S::NP + ((R16 - (S::NP % 16)) + 16) % 16;
+  static constexpr size_t smem = (size_t)CT * PITCH * sizeof(float2);
+};
+
+__device__ __forceinline__ float2 twiddle2(const ColArgs& a, long long e) {
+  e &= a.nmask;
+  const float2 hi = __ldg(a.tw_hi + (e >> a.tw_split));
+  const float2 lo = __ldg(a.tw_lo + (e & ((1LL << a.tw_split) - 1)));
+  return make_float2(hi.x * lo.x - hi.y * lo.y, hi.x * lo.y + hi.y * lo.x);
+}
+
+template <int LOGL, bool INV, int KIND>
+__global__ void __launch_bounds__(ColGeom<LOGL>::THREADS) k_col(ColArgs a) {
+  using GM = ColGeom<LOGL>;
+  using S = typename GM::S;
+  constexpr int L = GM::L;
+  constexpr int CT = GM::CT;
+  constexpr int THREADS = GM::THREADS;
+  extern __shared__ float2 sm2[];
+  const int tid = threadIdx.x;
+  const long long tile = blockIdx.x;
+  const long long ncb = (a.ncols + CT - 1) / CT;
+  const long long cb = tile % ncb;
+  const long long rest = tile / ncb;
+  const long long o1 = rest % a.O1;
+  const long long o2 = rest / a.O1;
+  const long long c0 = cb * CT;
+  const float* __restrict__ inr = a.xr + o2 * a.is_o2 + o1 * a.is_o1 + c0;
+  const float* __restrict__ ini = a.xi + o2 * a.is_o2 + o1 * a.is_o1 + c0;
+
+  // coalesced tile load: consecutive threads take consecutive columns
+  for (int idx = tid; idx < CT * L; idx += THREADS) {
+    const int c = idx % CT;
+    const int jj = idx / CT;
+    float2 v = make_float2(0.f, 0.f);
+    if (c0 + c < a.ncols) {
+      const long long off = (long long)jj * a.is_j + c;
+      v = make_float2(__ldg(inr + off), __ldg(ini + off));
+    }
+    sm2[c * GM::PITCH + spad<S::SH>(jj)] = v;
+  }
+  __syncthreads();
+  {
+    const int col = tid / S::T;
+    const int j = tid % S::T;
+    smem_passes<LOGL, GM::LE, INV, 0, S::P>(j, sm2 + col * GM::PITCH);
+  }
+  // twiddle + store
+  float* __restrict__ outr = a.yr + o2 * a.os_o2 + o1 * a.os_o1;
+  float* __restrict__ outi = a.yi + o2 * a.os_o2 + o1 * a.os_o1;
+  for (int idx = tid; idx < CT * L; idx += THREADS) {
+    int c, k;
+    if constexpr (KIND == 0) {
+      c = idx % CT;
+      k = idx / CT;
+    } else {
+      c = idx / L;
+      k = idx % L;
+    }
+    const long long cg = c0 + c;
+    if (cg >= a.ncols) continue;
+    float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
+    if (a.has_tw) {
+      const long long e = a.tw_mul * (o1 * (a.tw_a * cg + a.tw_b * k) + a.tw_c * cg * k);
+      float2 w = twiddle2(a, e);
+      if (INV) w.y = -w.y;
+      v = make_float2(v.x * w.x - v.y * w.y, v.x * w.y + v.y * w.x);
+    }
+    const long long off = (KIND == 0) ? (cg + (long long)k * a.os_k) : (cg * a.os_c + k);
+    outr[off] = v.x * a.scale;
+    outi[off] = v.y * a.scale;
+  }
+}
+
+template <int LOGL, bool INV, int KIND>
+static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
+  using GM = ColGeom<LOGL>;
+  auto kern = k_col<LOGL, INV, KIND>;
+  if (GM::smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
+    if (e != cudaSuccess) return e;
+  }
+  const long long ncb = (a.ncols + GM::CT - 1) / GM::CT;
+  const long long tiles = ncb * a.O1 * a.O2;
+  if (tiles <= 0) return cudaSuccess;
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  kern<<<(unsigned)tiles, GM::THREADS, GM::smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int LOGL>
+static cudaError_t launch_col_l(bool inv, int kind, const ColArgs& a, cudaStream_t st) {
+  if (kind == 0) return inv ? launch_col_t<LOGL, true, 0>(a, st) : launch_col_t<LOGL, false, 0>(a, st);
+  return inv ? launch_col_t<LOGL, true, 1>(a, st) : launch_col_t<LOGL, false, 1>(a, st);
+}
+
+cudaError_t launch_colpass(int logl, bool inv, int kind, const ColArgs& a, cudaStream_t st) {
+  switch (logl) {
+    case 1: return launch_col_l<1>(inv, kind, a, st);
+    case 2: return launch_col_l<2>(inv, kind, a, st);
+    case 3: return launch_col_l<3>(inv, kind, a, st);
+    case 4: return launch_col_l<4>(inv, kind, a, st);
+    case 5: return launch_col_l<5>(inv, kind, a, st);
+    case 6: return launch_col_l<6>(inv, kind, a, st);
+    case 7: return launch_col_l<7>(inv, kind, a, st);
+    case 8: return launch_col_l<8>(inv, kind, a, st);
+    case 9: return launch_col_l<9>(inv, kind, a, st);
+    case 10: return launch_col_l<10>(inv, kind, a, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tfb
