@@ -114,6 +114,24 @@ TRNFFT_API int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, cons
                                     float* out_re, float* out_im, int64_t outer, int64_t inner,
                                     int inverse, void* work, void* stream);
 
+/* In-place complex transform that allocates nothing, for callers that cannot
+ * call cudaMalloc or hand over a work area (code running inside another
+ * allocator or memory pool, real-time callbacks that must not allocate,
+ * runtimes that only lend fixed buffers).  No counterpart in the reference.
+ *
+ * Only power-of-two n > 4096 (the multi-pass sizes that need scratch) and
+ * batch * n <= 2^21 complex values: the scratch is a fixed 16 MiB device
+ * array that every GPU loading the library keeps until process exit.
+ * Larger requests fail with TRNFFT_INVALID_VALUE.  The first call on a device
+ * looks up the array's device address (make that first call before any
+ * stream capture).  All calls on a device share the one array, so calls
+ * whose work overlaps on the GPU (different streams, or different host
+ * threads without ordering) race and corrupt each other's results;
+ * serialise them.  The array keeps the last call's contents; nothing in it
+ * needs clearing because every call overwrites what it reads. */
+TRNFFT_API int trnfft_exec_c2c_inplace_noalloc(trnfft_plan_t plan, float* re, float* im, int64_t batch,
+                                               int inverse, void* stream);
+
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex
  * transform of the real row and keeps the first n//2+1 bins. */

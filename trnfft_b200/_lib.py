@@ -43,6 +43,7 @@ SIGNATURES = {
     "trnfft_plan_query": (_INT, [_P, ctypes.POINTER(_INT), ctypes.POINTER(_I64), _I64, ctypes.POINTER(_I64)]),
     "trnfft_exec_c2c": (_INT, [_P, _P, _P, _P, _P, _I64, _INT, _P, _P]),
     "trnfft_exec_c2c_axis": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _INT, _P, _P]),
+    "trnfft_exec_c2c_inplace_noalloc": (_INT, [_P, _P, _P, _I64, _INT, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
     "trnfft_exec_c2r": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
 }

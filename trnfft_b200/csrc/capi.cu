@@ -105,23 +105,15 @@ void host_fft_double(std::vector<std::complex<double>>& a) {
 }
 
 }  // namespace
+
+// Record a failure message for trnfft_last_error() from another translation unit.
+int record_failure(int code, const char* msg) { return fail(code, "%s", msg); }
+
 }  // namespace tfb
 
 using namespace tfb;
 
-struct trnfft_plan_s {
-  int64_t n = 0;
-  int device = 0;
-  int algorithm = TRNFFT_ALG_COPY;
-  int logn = -1;
-  int64_t m = 0;  // Bluestein padded length
-  int logm = -1;
-  float2* chirp = nullptr;  // Bluestein: n entries
-  float2* H = nullptr;      // Bluestein: m entries
-  float2* tw_hi = nullptr;  // power of two n > 1024: W_n^(i << tw_split)
-  float2* tw_lo = nullptr;  // power of two n > 1024: W_n^i, i < 2^tw_split
-  int tw_split = 0;
-};
+#include "plan_internal.h"
 
 // Two-level twiddle tables for W_n, n = 2^logn: W_n^e = hi[e >> s] * lo[e & (2^s - 1)].
 static int make_twiddle_tables(trnfft_plan_s* p) {

@@ -7,6 +7,8 @@
 
 namespace tfb {
 
+int record_failure(int code, const char* msg);
+
 // Rows of a batch, row r of the input at xr/xi + r*in_stride, of the output
 // at yr/yi + r*out_stride (strides in floats).
 struct RowArgs {

@@ -1,0 +1,21 @@
+// Definition of the opaque plan object behind trnfft_plan_t (internal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/trnfft_b200.h"
+
+struct trnfft_plan_s {
+  int64_t n = 0;
+  int device = 0;
+  int algorithm = TRNFFT_ALG_COPY;
+  int logn = -1;
+  int64_t m = 0;  // Bluestein padded length
+  int logm = -1;
+  float2* chirp = nullptr;  // Bluestein: n entries
+  float2* H = nullptr;      // Bluestein: m entries
+  float2* tw_hi = nullptr;  // power of two n > 1024: W_n^(i << tw_split)
+  float2* tw_lo = nullptr;  // power of two n > 1024: W_n^i, i < 2^tw_split
+  int tw_split = 0;
+};
