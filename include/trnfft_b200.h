@@ -132,6 +132,20 @@ TRNFFT_API int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, cons
 TRNFFT_API int trnfft_exec_c2c_inplace_noalloc(trnfft_plan_t plan, float* re, float* im, int64_t batch,
                                                int inverse, void* stream);
 
+/* Short-time Fourier transform of `batch` real signals of `length` samples,
+ * power-of-two n_fft = plan n (4..8192).  Replaces trnfft.stft
+ * (trnfft/api.py:291-365): frames start every `hop` samples of the signal
+ * padded by n_fft/2 on both sides when `center` (pad_mode 0 reflect,
+ * 1 constant, 2 replicate, 3 circular, as torch.nn.functional.pad), are
+ * multiplied by `window` (n_fft floats, already zero-padded to n_fft), and
+ * transformed; `normalized` scales by 1/sqrt(n_fft).  Output planes are
+ * (batch, bins, frames) with bins = n_fft/2+1 (onesided) or n_fft, and
+ * frames = 1 + (length + 2*pad - n_fft) / hop, which the caller passes as a
+ * check. */
+TRNFFT_API int trnfft_exec_stft(trnfft_plan_t plan, const float* signal, int64_t batch, int64_t length,
+                                int64_t hop, const float* window, int center, int pad_mode, int normalized,
+                                int onesided, int64_t frames, float* out_re, float* out_im, void* stream);
+
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex
  * transform of the real row and keeps the first n//2+1 bins. */

@@ -280,10 +280,12 @@ def _pad_signal(x2: torch.Tensor, p: int, pad_mode: str) -> torch.Tensor:
     return torch.nn.functional.pad(x2.unsqueeze(1), (p, p), mode=pad_mode).squeeze(1)
 
 
-def stft(x: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool, pad_mode: str,
-         normalized: bool, onesided: bool):
-    """Framing (trnfft/api.py:310-336), transform of each frame, (..., freq, time) layout."""
-    _check(x, "input")
+_PAD_MODES = {"reflect": 0, "constant": 1, "replicate": 2, "circular": 3}
+
+
+def _stft_composite(x, n_fft, hop, w, center, pad_mode, normalized, onesided):
+    """Framing with torch ops + the library transforms; used for autograd and for
+    n_fft the fused kernel does not cover."""
     lead = x.shape[:-1]
     L = x.shape[-1]
     x2 = x.reshape(-1, L)
@@ -302,6 +304,36 @@ def stft(x: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool, p
         yi = yi * sc
     nb, nf = yr.shape[-2], yr.shape[-1]
     return yr.reshape(*lead, nb, nf).contiguous(), yi.reshape(*lead, nb, nf).contiguous()
+
+
+def stft(x: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool, pad_mode: str,
+         normalized: bool, onesided: bool):
+    """STFT with output (..., freq, time) (trnfft/api.py:291-365)."""
+    _check(x, "input")
+    fused = (n_fft >= 4 and (n_fft & (n_fft - 1)) == 0 and n_fft <= 8192 and pad_mode in _PAD_MODES
+             and not _needs_grad(x, w))
+    if not fused:
+        return _stft_composite(x, n_fft, hop, w, center, pad_mode, normalized, onesided)
+    lead = x.shape[:-1]
+    L = x.shape[-1]
+    a = x.reshape(-1, L).contiguous()
+    B = a.shape[0]
+    pad = n_fft // 2 if center else 0
+    if center and pad_mode == "reflect" and pad >= L:
+        raise RuntimeError(f"stft: reflect padding {pad} must be smaller than the signal length {L}")
+    lp = L + 2 * pad
+    if lp < n_fft:
+        raise RuntimeError(f"stft: signal of {L} samples is shorter than n_fft={n_fft}")
+    nf = 1 + (lp - n_fft) // hop
+    nb = n_fft // 2 + 1 if onesided else n_fft
+    yr = torch.empty(B, nb, nf, dtype=torch.float32, device=a.device)
+    yi = torch.empty_like(yr)
+    if B:
+        plan = _lib.device_plan(n_fft, a.device)
+        _lib.call("trnfft_exec_stft", plan.handle, _lib.ptr(a), B, L, hop, _lib.ptr(w.contiguous()),
+                  int(bool(center)), _PAD_MODES[pad_mode], int(bool(normalized)), int(bool(onesided)), nf,
+                  _lib.ptr(yr), _lib.ptr(yi), _lib.stream_ptr(a.device))
+    return yr.reshape(*lead, nb, nf), yi.reshape(*lead, nb, nf)
 
 
 def istft(sr: torch.Tensor, si: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool,

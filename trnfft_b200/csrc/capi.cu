@@ -473,6 +473,35 @@ int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, const float* in
   return TRNFFT_SUCCESS;
 }
 
+int trnfft_exec_stft(trnfft_plan_t plan, const float* signal, int64_t batch, int64_t length, int64_t hop,
+                     const float* window, int center, int pad_mode, int normalized, int onesided,
+                     int64_t frames, float* out_re, float* out_im, void* stream) {
+  if (!plan) return fail(TRNFFT_INVALID_VALUE, "exec_stft: null plan");
+  const int64_t n = plan->n;
+  if (plan->logn < 2 || plan->logn > 13)
+    return fail(TRNFFT_UNSUPPORTED, "exec_stft: n_fft=%lld (power of two 4..8192 only)", (long long)n);
+  if (batch < 0 || length < 1 || hop < 1) return fail(TRNFFT_INVALID_VALUE, "exec_stft: bad batch/length/hop");
+  if (pad_mode < 0 || pad_mode > 3) return fail(TRNFFT_INVALID_VALUE, "exec_stft: bad pad_mode %d", pad_mode);
+  const int64_t pad = center ? n / 2 : 0;
+  if (center && pad_mode == 0 && pad >= length)
+    return fail(TRNFFT_INVALID_VALUE, "exec_stft: reflect padding %lld needs length > %lld", (long long)pad,
+                (long long)pad);
+  const int64_t lp = length + 2 * pad;
+  if (lp < n) return fail(TRNFFT_INVALID_VALUE, "exec_stft: signal shorter than n_fft");
+  const int64_t nf = 1 + (lp - n) / hop;
+  if (frames != nf) return fail(TRNFFT_INVALID_VALUE, "exec_stft: frames=%lld, expected %lld", (long long)frames, (long long)nf);
+  if (batch == 0) return TRNFFT_SUCCESS;
+  int rc = check_ptrs("exec_stft", {signal, window, out_re, out_im}, 4);
+  if (rc) return rc;
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_stft: cannot select device %d", plan->device);
+  StftArgs a{signal, window, out_re, out_im, batch, length, nf, hop, pad, pad_mode, onesided ? 1 : 0,
+             normalized ? (float)(1.0 / std::sqrt((double)n)) : 1.f};
+  cudaError_t e = launch_stft(plan->logn, a, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "exec_stft");
+  return TRNFFT_SUCCESS;
+}
+
 int trnfft_exec_r2c(trnfft_plan_t plan, const float* in, float* out_re, float* out_im,
                     int64_t batch, void* work, void* stream) {
   (void)work;

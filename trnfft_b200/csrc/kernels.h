@@ -63,6 +63,22 @@ struct ColArgs {
 
 cudaError_t launch_colpass(int logl, bool inv, int kind, const ColArgs& a, cudaStream_t st);
 
+// Fused STFT (stft.cu): frame f of waveform b covers padded samples
+// [f*hop, f*hop + n) = original [f*hop - pad, ...) mapped by pad_mode
+// (0 reflect, 1 constant, 2 replicate, 3 circular); output (batch, bins, frames).
+struct StftArgs {
+  const float* x;
+  const float* window;  // n_fft entries
+  float* yr;
+  float* yi;
+  long long batch, len, frames, hop, pad;
+  int pad_mode;
+  int onesided;
+  float scale;
+};
+
+cudaError_t launch_stft(int logn, const StftArgs& a, cudaStream_t st);
+
 cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st);
 bool rows_c2c_tma_ok(int logn, const RowArgs& a);
 cudaError_t launch_rows_c2c_tma(int logn, bool inv, const RowArgs& a, cudaStream_t st);
