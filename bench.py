@@ -176,62 +176,311 @@ def barrier(world):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the oracle restatement of the reference's radix-2 algorithm
+# Workloads.  Each names its config, builds device inputs, a step (one pass of
+# the hot path over one batch), its kernel launches, the work per step for
+# the metric, the algorithmic HBM bytes of the dominant launch, and a bounded
+# CPU sample of the same work on the oracle (the reference's algorithm).
 # ---------------------------------------------------------------------------
 
 
-def cpu_reference_sample(rows: int, threads: int, seed: int = 0):
-    """Times fft+ifft of `rows` rows of N=1024 with the oracle on `threads` threads."""
-    from oracle import trnfft_oracle as O
-
-    rng = np.random.default_rng(seed)
-    xr = rng.standard_normal((rows, N)).astype(np.float32)
-    xi = rng.standard_normal((rows, N)).astype(np.float32)
-
-    def step(a, b):
-        yr, yi = O.fft(a, b)
-        return O.ifft(yr, yi)
-
-    t0 = time.perf_counter()
-    O.threaded_rows(step, (xr, xi), threads)
-    return time.perf_counter() - t0
+def c2c_flops(n, batch):
+    return 5.0 * n * math.log2(n) * batch
 
 
-def cpu_baseline(budget_s: float = 10.0):
+class Workload:
+    metric = METRIC
+    unit = UNIT
+    dominant = None
+
+    def cpu_sample(self, threads):
+        raise NotImplementedError
+
+
+class C2CRoundTrip(Workload):
+    """fft then ifft of a (batch, n) planar complex batch (BASELINE configs[0] / [3])."""
+
+    def __init__(self, n, batch, tag):
+        self.n, self.batch, self.tag = n, batch, tag
+        self.name = f"batched C2C FFT+IFFT round trip, N={n}, batch={batch} per GPU ({tag})"
+        self.work = 2 * c2c_flops(n, batch)
+        self.dom_bytes = 16.0 * n * batch
+        alg = "Stockham" if n & (n - 1) == 0 else "fused Bluestein"
+        self.dominant = f"{alg} C2C kernel, N={n}"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+        from trnfft_b200 import ComplexTensor
+
+        self.xr = torch.randn(self.batch, self.n, device=dev, generator=g)
+        self.xi = torch.randn(self.batch, self.n, device=dev, generator=g)
+        x = ComplexTensor(self.xr, self.xi)
+        self.step = lambda: trnfft.ifft(trnfft.fft(x))
+        self.launches = {"fft": lambda: trnfft.fft(x), "ifft": lambda: trnfft.ifft(x)}
+        self.launches_per_step = 2
+        self.inputs = [self.xr, self.xi]
+
+        def from_inputs(ts):
+            y = trnfft.ifft(trnfft.fft(ComplexTensor(ts[0], ts[1])))
+            return [y.real, y.imag]
+
+        self.e2e_fn = from_inputs
+
+    def check(self, out):
+        return rel_err(out.real, self.xr)
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        rng = np.random.default_rng(0)
+        xr = rng.standard_normal((rows, self.n)).astype(np.float32)
+        xi = rng.standard_normal((rows, self.n)).astype(np.float32)
+        prec = "fast"
+
+        def f(a, b):
+            yr, yi = O.fft(a, b, precision=prec)
+            return O.ifft(yr, yi, precision=prec)
+
+        t0 = time.perf_counter()
+        O.threaded_rows(f, (xr, xi), threads)
+        return time.perf_counter() - t0, 2 * c2c_flops(self.n, rows)
+
+
+class SmallN(Workload):
+    """BASELINE configs[1](a): batch 262144 forward FFTs for each of N = 64, 128, 256."""
+
+    def __init__(self):
+        self.batch = 262144
+        self.ns = (64, 128, 256)
+        self.name = "small-N batched C2C FFT, N=64,128,256, batch=262144 each (configs[1]a)"
+        self.work = sum(c2c_flops(n, self.batch) for n in self.ns)
+        self.dom_bytes = 16.0 * 256 * self.batch
+        self.dominant = "Stockham C2C kernel, N=256"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+        from trnfft_b200 import ComplexTensor
+
+        self.xs = [ComplexTensor(torch.randn(self.batch, n, device=dev, generator=g),
+                                 torch.randn(self.batch, n, device=dev, generator=g)) for n in self.ns]
+        self.step = lambda: [trnfft.fft(x) for x in self.xs][-1]
+        self.launches = {"fft256": lambda: trnfft.fft(self.xs[-1])}
+        self.launches_per_step = 3
+        self.inputs = [t for x in self.xs for t in (x.real, x.imag)]
+
+        def from_inputs(ts):
+            outs = []
+            for k in range(3):
+                y = trnfft.fft(ComplexTensor(ts[2 * k], ts[2 * k + 1]))
+                outs += [y.real, y.imag]
+            return outs
+
+        self.e2e_fn = from_inputs
+
+    def check(self, out):
+        x = self.xs[-1]
+        ref = torch.fft.fft(torch.complex(x.real, x.imag))
+        return rel_err(torch.complex(out.real, out.imag), ref)
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        rng = np.random.default_rng(0)
+        t = 0.0
+        work = 0.0
+        for n in self.ns:
+            xr = rng.standard_normal((rows, n)).astype(np.float32)
+            xi = rng.standard_normal((rows, n)).astype(np.float32)
+            t0 = time.perf_counter()
+            O.threaded_rows(lambda a, b: O.fft(a, b), (xr, xi), threads)
+            t += time.perf_counter() - t0
+            work += c2c_flops(n, rows)
+        return t, work
+
+
+class Stft(Workload):
+    """256 waveforms x 160000 samples, n_fft 512, hop 256, Hann, reflect."""
+
+    metric = "STFT frames/s (256 x 160000 samples, n_fft 512, hop 256, onesided)"
+    unit = "frames/s"
+
+    def __init__(self):
+        self.B, self.L, self.nfft, self.hop = 256, 160000, 512, 256
+        self.frames = 1 + (self.L + 2 * (self.nfft // 2) - self.nfft) // self.hop
+        self.name = "STFT 256 x 160000 samples, n_fft=512, hop=256, periodic Hann, reflect (configs[2])"
+        self.work = float(self.B * self.frames)
+        self.dom_bytes = 4.0 * self.B * self.L + 8.0 * self.B * self.frames * (self.nfft // 2 + 1)
+        self.dominant = "fused STFT kernel (n_fft=512)"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+
+        t = torch.arange(self.L, device=dev, dtype=torch.float32) / 16000.0
+        x = torch.randn(self.B, self.L, device=dev, generator=g)
+        f = 50.0 + 6950.0 * torch.rand(self.B, 8, 1, device=dev, generator=g)
+        ph = 2 * math.pi * torch.rand(self.B, 8, 1, device=dev, generator=g)
+        x = x + torch.sin(2 * math.pi * f * t + ph).sum(1)
+        self.x = x.contiguous()
+        self.win = torch.hann_window(self.nfft, device=dev)
+        self.step = lambda: trnfft.stft(self.x, self.nfft, self.hop, window=self.win)
+        self.launches = {"stft": self.step}
+        self.launches_per_step = 1
+        self.inputs = [self.x]
+        self.e2e_fn = lambda ts: (lambda S: [S.real, S.imag])(
+            trnfft.stft(ts[0], self.nfft, self.hop, window=self.win))
+
+    def check(self, out):
+        ref = torch.stft(self.x[:8], self.nfft, self.hop, window=self.win, center=True, pad_mode="reflect",
+                         return_complex=True)
+        return rel_err(torch.complex(out.real[:8], out.imag[:8]), ref)
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        rng = np.random.default_rng(0)
+        w = rng.standard_normal((max(1, rows // 64), self.L)).astype(np.float32)
+        t0 = time.perf_counter()
+        O.threaded_rows(lambda a: O.stft(a, self.nfft, self.hop), (w,), threads)
+        return time.perf_counter() - t0, float(w.shape[0] * self.frames)
+
+
+class Large(Workload):
+    """one N = 2^30 complex transform (fft + ifft) on one GPU."""
+
+    def __init__(self, logn=30):
+        self.n = 1 << logn
+        self.name = f"single 1-D C2C FFT+IFFT, N=2^{logn} (8 GiB planar at 2^30) (configs[4], 1 GPU)"
+        self.work = 2 * c2c_flops(self.n, 1)
+        self.dom_bytes = 3 * 16.0 * self.n  # three column-tile passes, each reads and writes all data
+        self.dominant = "three column-tile passes (1024 x 1024 x 1024)"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+        from trnfft_b200 import ComplexTensor
+
+        self.xr = torch.randn(1, self.n, device=dev, generator=g)
+        self.xi = torch.randn(1, self.n, device=dev, generator=g)
+        x = ComplexTensor(self.xr, self.xi)
+        self.step = lambda: trnfft.ifft(trnfft.fft(x))
+        self.launches = {"fft": lambda: trnfft.fft(x)}
+        self.launches_per_step = 6
+        self.inputs = [self.xr, self.xi]
+        self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(trnfft.ifft(trnfft.fft(ComplexTensor(ts[0], ts[1]))))
+
+    def check(self, out):
+        return rel_err(out.real, self.xr)
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        n = 1 << 20
+        rng = np.random.default_rng(0)
+        xr = rng.standard_normal(n).astype(np.float32)
+        xi = rng.standard_normal(n).astype(np.float32)
+        t0 = time.perf_counter()
+        O.stage_parallel_fft(xr, xi, False)
+        return time.perf_counter() - t0, c2c_flops(n, 1)
+
+
+class Fft2(Workload):
+    """BASELINE configs[4] second part: fft2 of a 16384 x 16384 complex field (1 GPU)."""
+
+    def __init__(self, side=16384):
+        self.s = side
+        self.name = f"fft2 of a {side}x{side} complex fp32 field (configs[4], 1 GPU)"
+        self.work = 2 * c2c_flops(side, side)
+        self.dom_bytes = 4 * 16.0 * side * side
+        self.dominant = "row passes + strided column passes"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+        from trnfft_b200 import ComplexTensor
+
+        self.xr = torch.randn(self.s, self.s, device=dev, generator=g)
+        self.xi = torch.randn(self.s, self.s, device=dev, generator=g)
+        x = ComplexTensor(self.xr, self.xi)
+        self.step = lambda: trnfft.fft2(x)
+        self.launches = {"fft2": self.step}
+        self.launches_per_step = 4
+        self.inputs = [self.xr, self.xi]
+        self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(trnfft.fft2(ComplexTensor(ts[0], ts[1])))
+
+    def check(self, out):
+        ref = torch.fft.fft2(torch.complex(self.xr, self.xi))
+        return rel_err(torch.complex(out.real, out.imag), ref)
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        s = 1024
+        rng = np.random.default_rng(0)
+        xr = rng.standard_normal((s, s)).astype(np.float32)
+        xi = rng.standard_normal((s, s)).astype(np.float32)
+        t0 = time.perf_counter()
+        O.fft2(xr, xi)
+        return time.perf_counter() - t0, 2 * c2c_flops(s, s)
+
+
+WORKLOADS = {
+    "c2c1024": lambda: C2CRoundTrip(N, BATCH, "BASELINE configs[0]"),
+    "smalln": SmallN,
+    "stft": Stft,
+    "bluestein4093": lambda: C2CRoundTrip(4093, 4096, "BASELINE configs[3]"),
+    "bluestein1000": lambda: C2CRoundTrip(1000, 4096, "BASELINE configs[3]"),
+    "bluestein6000": lambda: C2CRoundTrip(6000, 4096, "BASELINE configs[3]"),
+    "large": Large,
+    "fft2": Fft2,
+}
+
+
+def cpu_rate(wl, threads, budget_s, rows=256):
+    wl.cpu_sample(threads, max(8, rows // 8))  # warm-up
+    t_total, w_total, reps = 0.0, 0.0, 0
+    while t_total < budget_s:
+        t, w = wl.cpu_sample(threads, rows)
+        t_total += t
+        w_total += w
+        reps += 1
+        if t > budget_s:
+            break
+    return w_total / t_total, t_total, reps
+
+
+def scale_value(v, unit):
+    return v / 1e9 if unit == UNIT else v
+
+
+def cpu_baseline(wl, budget_s):
     threads = os.cpu_count() or 1
-    rows = 512
-    cpu_reference_sample(64, threads)  # warm-up
-    done, elapsed = 0, 0.0
-    while elapsed < budget_s:
-        elapsed += cpu_reference_sample(rows, threads, seed=done)
-        done += rows
-    value = flops_per_step(N, done) / elapsed / 1e9
-    return {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"oracle/trnfft_oracle.py radix-2 fft+ifft, N={N}, {done} rows "
-                      f"(of {BATCH} per step) in {elapsed:.1f} s on {threads} threads"}
+    rate, t, reps = cpu_rate(wl, threads, budget_s)
+    return {"value": round(scale_value(rate, wl.unit), 4), "unit": wl.unit, "cores": threads, "kind": "port",
+            "sample": f"oracle/trnfft_oracle.py ({wl.name}), {reps} bounded sample(s) in {t:.1f} s "
+                      f"on {threads} host threads"}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
+    wl = WORKLOADS[args.workload]()
     threads = os.cpu_count() or 1
-    rows = 256
     for _ in range(args.warmup):
-        cpu_reference_sample(rows, threads)
-    times = [cpu_reference_sample(rows, threads, seed=k) for k in range(args.steps)]
-    ms = 1000.0 * sum(times) / len(times) * (BATCH / rows)  # per full step of BATCH rows
-    value = flops_per_step(N, rows) / (sum(times) / len(times)) / 1e9
+        wl.cpu_sample(threads, 64)
+    times, works = [], []
+    for _ in range(args.steps):
+        t, w = wl.cpu_sample(threads, 256)
+        times.append(t)
+        works.append(w)
+    rate = sum(works) / sum(times)
+    value = round(scale_value(rate, wl.unit), 4)
     out = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1000.0 * wl.work / rate, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"batched C2C FFT+IFFT round trip, N={N}, batch={BATCH} per GPU "
-                               "(BASELINE configs[0]); each step times a bounded sample of "
-                               f"{rows} rows and reports the rate", "parallelism": "host threads"},
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows of N={N} fft+ifft per step, oracle/trnfft_oracle.py"},
-        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": {"workload": wl.name + "; each step times a bounded sample and reports the rate",
+                   "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
+                         "sample": "bounded sample per step, oracle/trnfft_oracle.py (the reference's algorithm)"},
+        "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
 
@@ -242,14 +491,11 @@ def run_reference(args, world, rank):
 
 
 def run_ours(args, world, rank, local):
-    import trnfft_b200 as trnfft
-    from trnfft_b200 import ComplexTensor
-
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    xr = torch.randn(BATCH, N, device=dev, generator=g)
-    xi = torch.randn(BATCH, N, device=dev, generator=g)
+    wl = WORKLOADS[args.workload]()
+    wl.setup(dev, g)
     flush = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     flush_out = torch.empty(1, dtype=torch.float32, device=dev)
 
@@ -257,14 +503,9 @@ def run_ours(args, world, rank, local):
         # read-only sweep of a buffer twice the L2 size: evicts every line
         # (dirty lines are written back here, not inside the timed kernel)
         torch.sum(flush, dim=0, keepdim=True, out=flush_out)
-    x = ComplexTensor(xr, xi)
-
-    def step():
-        y = trnfft.fft(x)
-        return trnfft.ifft(y)
 
     for _ in range(max(args.warmup, 3)):
-        step()
+        wl.step()
     torch.cuda.synchronize()
 
     # The step (and each launch alone) is captured once as a CUDA graph, so the
@@ -272,15 +513,18 @@ def run_ours(args, world, rank, local):
     # replay the L2 is flushed; the flush is enqueued first so the GPU is busy
     # while the events and the replay are queued behind it.
     st = torch.cuda.current_stream(dev)
-    g_step, g_fft, g_ifft = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    g_step = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_step):
-        y_step = step()
-    with torch.cuda.graph(g_fft):
-        y_fft = trnfft.fft(x)
-    with torch.cuda.graph(g_ifft):
-        y_ifft = trnfft.ifft(x)
-    for g in (g_step, g_fft, g_ifft):
-        g.replay()
+        y_step = wl.step()
+    g_launch = {}
+    for k, fn in wl.launches.items():
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gg):
+            fn()
+        g_launch[k] = gg
+    g_step.replay()
+    for gg in g_launch.values():
+        gg.replay()
     torch.cuda.synchronize()
 
     def timed(graph):
@@ -294,8 +538,8 @@ def run_ours(args, world, rank, local):
 
     launch_ms = []
     for _ in range(max(3, args.steps // 2)):
-        launch_ms.append(timed(g_fft))
-        launch_ms.append(timed(g_ifft))
+        for gg in g_launch.values():
+            launch_ms.append(timed(gg))
 
     barrier(world)
     torch.cuda.synchronize()
@@ -303,34 +547,28 @@ def run_ours(args, world, rank, local):
         step_ms = [timed(g_step) for _ in range(args.steps)]
         torch.cuda.synchronize()
     barrier(world)
-    ms_local = sum(step_ms) / len(step_ms)
-    ms = allreduce_max(ms_local, world)
-    value = world * flops_per_step() / (ms / 1e3) / 1e9
-    ok = rel_err(y_step.real, xr) < 1e-5 and rel_err(y_fft.real, torch.fft.fft(torch.complex(xr, xi)).real) < 1e-5
+    ms = allreduce_max(sum(step_ms) / len(step_ms), world)
+    value = world * wl.work / (ms / 1e3)
+    err = wl.check(y_step)
 
-    # end to end: pinned host inputs -> device -> fft -> ifft -> pinned host result
-    hr = torch.empty(BATCH, N, dtype=torch.float32, pin_memory=True)
-    hi = torch.empty(BATCH, N, dtype=torch.float32, pin_memory=True)
-    hr.copy_(xr.cpu())
-    hi.copy_(xi.cpu())
-    outr = torch.empty_like(hr, pin_memory=True)
-    outi = torch.empty_like(hi, pin_memory=True)
-    dr = torch.empty_like(xr)
-    di = torch.empty_like(xi)
+    # end to end through the public API: pinned host inputs -> device -> step -> pinned host results
+    del g_step, g_launch
+    host_in = [t.cpu().pin_memory() for t in wl.inputs]
+    dev_in = [torch.empty_like(t) for t in wl.inputs]
+    outs = wl.e2e_fn(dev_in)
+    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
 
     def e2e_step():
-        dr.copy_(hr, non_blocking=True)
-        di.copy_(hi, non_blocking=True)
-        y = trnfft.ifft(trnfft.fft(ComplexTensor(dr, di)))
-        outr.copy_(y.real, non_blocking=True)
-        outi.copy_(y.imag, non_blocking=True)
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        for h, o in zip(host_out, wl.e2e_fn(dev_in)):
+            h.copy_(o, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
+    e2e_step()
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = []
-    for _ in range(args.steps):
+    for _ in range(max(3, min(args.steps, 10))):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         e2e_step()
@@ -339,39 +577,35 @@ def run_ours(args, world, rank, local):
         e2e_ms.append(e0.elapsed_time(e1))
     barrier(world)
     e2e_max = allreduce_max(sum(e2e_ms) / len(e2e_ms), world)
-    e2e_value = world * flops_per_step() / (e2e_max / 1e3) / 1e9
-
-    err = rel_err(y_step.real, xr)
+    e2e_value = world * wl.work / (e2e_max / 1e3)
 
     if rank != 0:
         return
     peak, peak_kind = measured_peaks()
     avg_launch = sum(launch_ms) / len(launch_ms)
-    achieved = algorithmic_bytes_per_launch() / (avg_launch / 1e3) / 1e9
+    achieved = wl.dom_bytes / (avg_launch / 1e3) / 1e9
     out = {
-        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "metric": wl.metric, "value": round(scale_value(value, wl.unit), 3), "unit": wl.unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": f"batched C2C FFT+IFFT round trip, N={N}, batch={BATCH} per GPU "
-                               "(BASELINE configs[0])",
-                   "global_batch": BATCH * world, "seq_len": N, "parallelism": f"batch-sharded x{world}",
+        "config": {"workload": wl.name, "parallelism": f"batch-sharded x{world}" if world > 1 else "1 GPU",
                    "l2": "flushed before every timed step (256 MiB read sweep)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                     "traffic": profiled_traffic("k_c2c_n1024_b8192"),
-                     "kernel": "k_c2c<10,5> (Stockham radix 32-32)",
-                     "algorithmic_bytes_per_launch": algorithmic_bytes_per_launch(),
-                     "avg_launch_ms": round(avg_launch, 5)},
-        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "ms_per_step": round(e2e_max, 4),
-                "h2d_bytes_per_step": 2 * BATCH * N * 4, "d2h_bytes_per_step": 2 * BATCH * N * 4},
-        "gpu_launches": 2 * args.steps,
+                     "traffic": profiled_traffic(args.workload), "kernel": wl.dominant,
+                     "algorithmic_bytes_per_launch": wl.dom_bytes, "avg_launch_ms": round(avg_launch, 5)},
+        "e2e": {"value": round(scale_value(e2e_value, wl.unit), 3), "unit": wl.unit,
+                "ms_per_step": round(e2e_max, 4),
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
+                "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out)},
+        "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk.summary(),
-        "roundtrip_rel_l2": err, "parity_ok": bool(ok),
+        "check_rel_l2": err, "parity_ok": bool(err < 1e-5),
         "timing": "CUDA events around CUDA-graph replays of the step; L2 flushed before each",
     }
-    if world == 1:
-        out["cpu_baseline"] = cpu_baseline(args.cpu_budget)
+    if world == 1 and args.cpu_budget > 0:
+        out["cpu_baseline"] = cpu_baseline(wl, args.cpu_budget)
     print(json.dumps(out), flush=True)
 
 
@@ -382,6 +616,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2c1024")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:

@@ -28,26 +28,30 @@ struct ColGeom {
   static constexpr int CT0 = 256 / S::T;
   static constexpr int CT = CT0 < 8 ? 8 : (CT0 > 64 ? 64 : CT0);
   static constexpr int THREADS = CT * S::T;
+  static constexpr int MINB = THREADS >= 1024 ? 1 : 1024 / THREADS;  // >= 1024 resident threads per SM
   // column pitch in float2: CT columns of one half-warp land in distinct banks
   static constexpr int R16 = CT >= 16 ? 1 : 16 / CT;
   static constexpr int PITCH = S::NP + ((R16 - (S::NP % 16)) + 16) % 16;
   static constexpr size_t smem = (size_t)CT * PITCH * sizeof(float2);
 };
 
-__device__ __forceinline__ float2 twiddle2(const ColArgs& a, long long e) {
-  e &= a.nmask;
+// W_N^e for e already reduced mod N (N = 2^logN <= 2^30): two-level table.
+__device__ __forceinline__ float2 twiddle2(const ColArgs& a, uint32_t e) {
   const float2 hi = __ldg(a.tw_hi + (e >> a.tw_split));
-  const float2 lo = __ldg(a.tw_lo + (e & ((1LL << a.tw_split) - 1)));
+  const float2 lo = __ldg(a.tw_lo + (e & ((1u << a.tw_split) - 1u)));
   return make_float2(hi.x * lo.x - hi.y * lo.y, hi.x * lo.y + hi.y * lo.x);
 }
 
 template <int LOGL, bool INV, int KIND>
-__global__ void __launch_bounds__(ColGeom<LOGL>::THREADS) k_col(ColArgs a) {
+__global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k_col(ColArgs a) {
   using GM = ColGeom<LOGL>;
   using S = typename GM::S;
   constexpr int L = GM::L;
   constexpr int CT = GM::CT;
   constexpr int THREADS = GM::THREADS;
+  constexpr int ITER = CT * L / THREADS;  // elements per thread in the tile load/store
+  constexpr int RSTEP = THREADS / CT;     // rows advanced per iteration (column-wise mapping)
+  static_assert(THREADS % CT == 0 && (CT * L) % THREADS == 0, "tile mapping");
   extern __shared__ float2 sm2[];
   const int tid = threadIdx.x;
   const long long tile = blockIdx.x;
@@ -57,19 +61,26 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS) k_col(ColArgs a) {
   const long long o1 = rest % a.O1;
   const long long o2 = rest / a.O1;
   const long long c0 = cb * CT;
-  const float* __restrict__ inr = a.xr + o2 * a.is_o2 + o1 * a.is_o1 + c0;
-  const float* __restrict__ ini = a.xi + o2 * a.is_o2 + o1 * a.is_o1 + c0;
 
-  // coalesced tile load: consecutive threads take consecutive columns
-  for (int idx = tid; idx < CT * L; idx += THREADS) {
-    const int c = idx % CT;
-    const int jj = idx / CT;
-    float2 v = make_float2(0.f, 0.f);
-    if (c0 + c < a.ncols) {
-      const long long off = (long long)jj * a.is_j + c;
-      v = make_float2(__ldg(inr + off), __ldg(ini + off));
+  // ---- tile load: thread owns column cl and rows r0 + i*RSTEP; every load is
+  // issued before the first shared-memory store.
+  const int cl = tid % CT;
+  const int r0 = tid / CT;
+  const bool colok = c0 + cl < a.ncols;
+  {
+    const long long base = o2 * a.is_o2 + o1 * a.is_o1 + c0 + cl + (long long)r0 * a.is_j;
+    const float* __restrict__ pr = a.xr + base;
+    const float* __restrict__ pi = a.xi + base;
+    const long long step = (long long)RSTEP * a.is_j;
+    float vr[ITER], vi[ITER];
+#pragma unroll
+    for (int i = 0; i < ITER; ++i) {
+      vr[i] = colok ? __ldg(pr + i * step) : 0.f;
+      vi[i] = colok ? __ldg(pi + i * step) : 0.f;
     }
-    sm2[c * GM::PITCH + spad<S::SH>(jj)] = v;
+    float2* dst = sm2 + cl * GM::PITCH;
+#pragma unroll
+    for (int i = 0; i < ITER; ++i) dst[spad<S::SH>(r0 + i * RSTEP)] = make_float2(vr[i], vi[i]);
   }
   __syncthreads();
   {
@@ -77,30 +88,56 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS) k_col(ColArgs a) {
     const int j = tid % S::T;
     smem_passes<LOGL, GM::LE, INV, 0, S::P>(j, sm2 + col * GM::PITCH);
   }
-  // twiddle + store
-  float* __restrict__ outr = a.yr + o2 * a.os_o2 + o1 * a.os_o1;
-  float* __restrict__ outi = a.yi + o2 * a.os_o2 + o1 * a.os_o1;
-  for (int idx = tid; idx < CT * L; idx += THREADS) {
-    int c, k;
-    if constexpr (KIND == 0) {
-      c = idx % CT;
-      k = idx / CT;
-    } else {
-      c = idx / L;
-      k = idx % L;
-    }
-    const long long cg = c0 + c;
-    if (cg >= a.ncols) continue;
-    float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
+
+  // ---- twiddle + store.  The exponent for output k of column cg is
+  // e = tw_mul*(o1*(tw_a*cg + tw_b*k) + tw_c*cg*k) = A1*cg + k*(B1 + C1*cg),
+  // evaluated mod 2^32 and then reduced mod N (N divides 2^32).
+  const uint32_t nmask = (uint32_t)a.nmask;
+  const uint32_t A1 = (uint32_t)(a.tw_mul * o1 * a.tw_a);
+  const uint32_t B1 = (uint32_t)(a.tw_mul * o1 * a.tw_b);
+  const uint32_t C1 = (uint32_t)(a.tw_mul * a.tw_c);
+  auto twiddled = [&](float2 v, uint32_t cg, uint32_t k) {
     if (a.has_tw) {
-      const long long e = a.tw_mul * (o1 * (a.tw_a * cg + a.tw_b * k) + a.tw_c * cg * k);
-      float2 w = twiddle2(a, e);
+      float2 w = twiddle2(a, (A1 * cg + k * (B1 + C1 * cg)) & nmask);
       if (INV) w.y = -w.y;
       v = make_float2(v.x * w.x - v.y * w.y, v.x * w.y + v.y * w.x);
     }
-    const long long off = (KIND == 0) ? (cg + (long long)k * a.os_k) : (cg * a.os_c + k);
-    outr[off] = v.x * a.scale;
-    outi[off] = v.y * a.scale;
+    return make_float2(v.x * a.scale, v.y * a.scale);
+  };
+  if constexpr (KIND == 0) {
+    // column-wise, same thread mapping as the load
+    if (colok) {
+      const long long cg = c0 + cl;
+      const long long base = o2 * a.os_o2 + o1 * a.os_o1 + cg + (long long)r0 * a.os_k;
+      float* __restrict__ qr = a.yr + base;
+      float* __restrict__ qi = a.yi + base;
+      const long long step = (long long)RSTEP * a.os_k;
+      const float2* src = sm2 + cl * GM::PITCH;
+#pragma unroll
+      for (int i = 0; i < ITER; ++i) {
+        const int k = r0 + i * RSTEP;
+        const float2 v = twiddled(src[spad<S::SH>(k)], (uint32_t)cg, (uint32_t)k);
+        qr[i * step] = v.x;
+        qi[i * step] = v.y;
+      }
+    }
+  } else {
+    // row-wise: consecutive threads take consecutive k of one column
+    float* __restrict__ qr0 = a.yr + o2 * a.os_o2 + o1 * a.os_o1;
+    float* __restrict__ qi0 = a.yi + o2 * a.os_o2 + o1 * a.os_o1;
+#pragma unroll
+    for (int i = 0; i < ITER; ++i) {
+      const int idx = i * THREADS + tid;
+      const int c = idx >> LOGL;
+      const int k = idx & (L - 1);
+      const long long cg = c0 + c;
+      if (cg < a.ncols) {
+        const float2 v = twiddled(sm2[c * GM::PITCH + spad<S::SH>(k)], (uint32_t)cg, (uint32_t)k);
+        const long long off = cg * a.os_c + k;
+        qr0[off] = v.x;
+        qi0[off] = v.y;
+      }
+    }
   }
 }
 
