@@ -145,6 +145,8 @@ static ColArgs col_base(const trnfft_plan_s* p) {
   std::memset(&c, 0, sizeof c);
   c.O1 = 1;
   c.O2 = 1;
+  c.O3 = 1;
+  c.tw_modo = int64_t(1) << 62;
   c.scale = 1.f;
   c.nmask = p->n - 1;
   c.tw_split = p->tw_split;
@@ -157,52 +159,82 @@ static ColArgs col_base(const trnfft_plan_s* p) {
 static constexpr int kMaxColLog = 10;  // column passes transform up to 1024 points on chip
 static constexpr int kMaxMultipassLog = 30;
 
-// Contiguous rows of n = 2^p > 4096 points, out of place (in != out):
-// p <= 20: n = N1*N3 (n = n1 + N1*n3, k = k3 + N3*k1), two passes;
-// p <= 30: n = N1*N2*N3 (n = n1 + N1*n2 + N1*N2*n3, k = k3 + N3*k2 + N3*N2*k1), three passes.
+static constexpr int kMaxDigitLog = 8;  // multi-pass digits of at most 256 points
+
+// Contiguous rows of n = 2^p > 4096 points, out of place (in != out).
+// n is split into m digits N_1..N_m (each <= 256 points; n = n_1 + N_1 n_2 +
+// ... with n_1 fastest) and the output index is k = k_m + N_m (k_{m-1} + ...).
+// Pass 1 transforms the slowest digit n_m and stores rows [n_1]...[n_{m-1}][k_m]
+// (the transposing pass); passes 2..m transform n_{m-1}, ..., n_1 in place.
+// After transforming digit j >= 2 the values are multiplied by
+// W_N^{n_{j-1} * K_j * P_{j-1}}, K_j = sum_{i >= j} k_i Q_i, P_i = N_1..N_{i-1},
+// Q_i = N_{i+1}..N_m: the twiddles of the Cooley-Tukey recursion on the
+// leading digit, applied inside the pass that produces their operand.
 static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr,
                                       float* yi, int64_t batch, bool inv, cudaStream_t st) {
   const int L = p->logn;
   const long long N = p->n;
+  const int m = (L + kMaxDigitLog - 1) / kMaxDigitLog;
+  if (m < 2 || m > 4) return cudaErrorInvalidValue;
+  int lg[5] = {0, 0, 0, 0, 0};  // lg[1..m]
+  for (int i = 1; i <= m; ++i) lg[i] = L / m + (i <= L % m ? 1 : 0);
+  long long Nd[5], P[6];
+  P[1] = 1;
+  for (int i = 1; i <= m; ++i) {
+    Nd[i] = 1LL << lg[i];
+    P[i + 1] = P[i] * Nd[i];
+  }
+  auto Q = [&](int i) {  // N_{i+1} ... N_m
+    long long q = 1;
+    for (int t = i + 1; t <= m; ++t) q *= Nd[t];
+    return q;
+  };
   const float sc = inv ? (float)(1.0 / (double)N) : 1.f;
   cudaError_t e;
-  if (L <= 2 * kMaxColLog) {
-    const int l1 = L / 2, l3 = L - l1;
-    const long long N1 = 1LL << l1, N3 = 1LL << l3;
-    ColArgs a = col_base(p);  // FFT over n3, columns n1, rows n1*N3 + k3, twiddle W_N^{n1*k3}
+  {
+    // pass 1: FFT over n_m (stride P_m).  Columns n_1; outer digits:
+    // o1 = n_{m-1} (the twiddle digit), o2 = the digits n_2..n_{m-2} (m = 4: n_2), o3 = batch.
+    ColArgs a = col_base(p);
     a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
-    a.ncols = N1; a.O2 = batch; a.is_o2 = N; a.is_j = N1;
-    a.os_o2 = N; a.os_c = N3;
-    a.has_tw = 1; a.tw_c = 1;
-    e = launch_colpass(l3, inv, 1, a, st);
+    a.ncols = Nd[1];
+    a.is_j = P[m];
+    // output position of (n_1, ..., n_{m-1}, k_m) is sum_{i<m} n_i * (N_{i+1}..N_m) + k_m = n_i * Q(i)
+    a.os_c = Q(1);
+    if (m == 2) {
+      a.O1 = 1;
+      a.O2 = 1;
+      a.has_tw = 1; a.tw_c = 1;  // W_N^{n_1 k_2}
+    } else {
+      a.O1 = Nd[m - 1]; a.is_o1 = P[m - 1]; a.os_o1 = Q(m - 1);
+      a.has_tw = 1; a.tw_mul = P[m - 1]; a.tw_b = 1;  // W_N^{n_{m-1} k_m P_{m-1}}
+      if (m == 4) {
+        a.O2 = Nd[2]; a.is_o2 = P[2]; a.os_o2 = Q(2);
+      }
+    }
+    a.O3 = batch; a.is_o3 = N; a.os_o3 = N;
+    e = launch_colpass(lg[m], inv, 1, a, st);
     if (e != cudaSuccess) return e;
-    ColArgs b = col_base(p);  // FFT over n1 in place, columns k3
-    b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
-    b.ncols = N3; b.O2 = batch; b.is_o2 = N; b.is_j = N3;
-    b.os_o2 = N; b.os_k = N3; b.scale = sc;
-    return launch_colpass(l1, inv, 0, b, st);
   }
-  const int l1 = L / 3, l2 = (L - l1) / 2, l3 = L - l1 - l2;
-  const long long N1 = 1LL << l1, N2 = 1LL << l2, N3 = 1LL << l3;
-  ColArgs a = col_base(p);  // FFT over n3; columns n1, outer n2; rows (n1*N2 + n2)*N3 + k3
-  a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
-  a.ncols = N1; a.O1 = N2; a.O2 = batch; a.is_o1 = N1; a.is_o2 = N; a.is_j = N1 * N2;
-  a.os_o1 = N3; a.os_o2 = N; a.os_c = N2 * N3;
-  a.has_tw = 1; a.tw_mul = N1; a.tw_b = 1;  // W_{N2 N3}^{n2 k3} = W_N^{N1 n2 k3}
-  e = launch_colpass(l3, inv, 1, a, st);
-  if (e != cudaSuccess) return e;
-  ColArgs b = col_base(p);  // FFT over n2 in place; columns k3, outer n1; twiddle W_N^{n1 (k3 + N3 k2)}
-  b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
-  b.ncols = N3; b.O1 = N1; b.O2 = batch; b.is_o1 = N2 * N3; b.is_o2 = N; b.is_j = N3;
-  b.os_o1 = N2 * N3; b.os_o2 = N; b.os_k = N3;
-  b.has_tw = 1; b.tw_a = 1; b.tw_b = N3;
-  e = launch_colpass(l2, inv, 0, b, st);
-  if (e != cudaSuccess) return e;
-  ColArgs c = col_base(p);  // FFT over n1 in place; columns (k2, k3)
-  c.xr = yr; c.xi = yi; c.yr = yr; c.yi = yi;
-  c.ncols = N2 * N3; c.O2 = batch; c.is_o2 = N; c.is_j = N2 * N3;
-  c.os_o2 = N; c.os_k = N2 * N3; c.scale = sc;
-  return launch_colpass(l1, inv, 0, c, st);
+  for (int j = m - 1; j >= 1; --j) {
+    // in place, layout [n_1..n_{j-1}][n_j][k_{j+1}..k_m]: FFT over n_j (stride Q(j)),
+    // columns = the already transformed fast digits (Q(j) of them), outer = slow digits.
+    ColArgs b = col_base(p);
+    b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
+    b.ncols = Q(j);
+    b.is_j = Q(j);
+    b.os_k = Q(j);
+    b.O1 = P[j]; b.is_o1 = Nd[j] * Q(j); b.os_o1 = Nd[j] * Q(j);
+    b.O3 = batch; b.is_o3 = N; b.os_o3 = N;
+    if (j >= 2) {
+      // W_N^{n_{j-1} (k_j Q(j) + c) P_{j-1}}; n_{j-1} is the fastest digit of o1
+      b.has_tw = 1; b.tw_modo = Nd[j - 1]; b.tw_mul = P[j - 1]; b.tw_a = 1; b.tw_b = Q(j);
+    } else {
+      b.scale = sc;
+    }
+    e = launch_colpass(lg[j], inv, 0, b, st);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 // Transforms along the middle axis of an [outer][n][inner] array, inner > 1.
@@ -214,8 +246,8 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
   if (L <= kMaxColLog) {
     ColArgs a = col_base(p);
     a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
-    a.ncols = inner; a.O2 = outer; a.is_o2 = n * inner; a.is_j = inner;
-    a.os_o2 = n * inner; a.os_k = inner; a.scale = sc;
+    a.ncols = inner; a.O3 = outer; a.is_o3 = n * inner; a.is_j = inner;
+    a.os_o3 = n * inner; a.os_k = inner; a.scale = sc;
     return launch_colpass(L, inv, 0, a, st);
   }
   // n = L1*L2, point n1 + L1*n2, output k2 + L2*k1 (out of place first pass)
@@ -223,15 +255,15 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
   const long long L1 = 1LL << l1, L2 = 1LL << l2;
   ColArgs a = col_base(p);  // FFT over n2; outer n1; output (n1*L2 + k2)*S + s; twiddle W_n^{n1 k2}
   a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
-  a.ncols = inner; a.O1 = L1; a.O2 = outer; a.is_o1 = inner; a.is_o2 = n * inner; a.is_j = L1 * inner;
-  a.os_o1 = L2 * inner; a.os_o2 = n * inner; a.os_k = inner;
+  a.ncols = inner; a.O1 = L1; a.O3 = outer; a.is_o1 = inner; a.is_o3 = n * inner; a.is_j = L1 * inner;
+  a.os_o1 = L2 * inner; a.os_o3 = n * inner; a.os_k = inner;
   a.has_tw = 1; a.tw_b = 1;
   cudaError_t e = launch_colpass(l2, inv, 0, a, st);
   if (e != cudaSuccess) return e;
   ColArgs b = col_base(p);  // FFT over n1 in place; outer k2
   b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
-  b.ncols = inner; b.O1 = L2; b.O2 = outer; b.is_o1 = inner; b.is_o2 = n * inner; b.is_j = L2 * inner;
-  b.os_o1 = inner; b.os_o2 = n * inner; b.os_k = L2 * inner; b.scale = sc;
+  b.ncols = inner; b.O1 = L2; b.O3 = outer; b.is_o1 = inner; b.is_o3 = n * inner; b.is_j = L2 * inner;
+  b.os_o1 = inner; b.os_o3 = n * inner; b.os_k = L2 * inner; b.scale = sc;
   return launch_colpass(l1, inv, 0, b, st);
 }
 

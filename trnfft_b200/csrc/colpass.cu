@@ -57,10 +57,14 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   const long long tile = blockIdx.x;
   const long long ncb = (a.ncols + CT - 1) / CT;
   const long long cb = tile % ncb;
-  const long long rest = tile / ncb;
+  long long rest = tile / ncb;
   const long long o1 = rest % a.O1;
-  const long long o2 = rest / a.O1;
+  rest /= a.O1;
+  const long long o2 = rest % a.O2;
+  const long long o3 = rest / a.O2;
   const long long c0 = cb * CT;
+  const long long ibase = o1 * a.is_o1 + o2 * a.is_o2 + o3 * a.is_o3;
+  const long long obase = o1 * a.os_o1 + o2 * a.os_o2 + o3 * a.os_o3;
 
   // ---- tile load: thread owns column cl and rows r0 + i*RSTEP; every load is
   // issued before the first shared-memory store.
@@ -68,7 +72,7 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   const int r0 = tid / CT;
   const bool colok = c0 + cl < a.ncols;
   {
-    const long long base = o2 * a.is_o2 + o1 * a.is_o1 + c0 + cl + (long long)r0 * a.is_j;
+    const long long base = ibase + c0 + cl + (long long)r0 * a.is_j;
     const float* __restrict__ pr = a.xr + base;
     const float* __restrict__ pi = a.xi + base;
     const long long step = (long long)RSTEP * a.is_j;
@@ -91,51 +95,97 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
 
   // ---- twiddle + store.  The exponent for output k of column cg is
   // e = tw_mul*(o1*(tw_a*cg + tw_b*k) + tw_c*cg*k) = A1*cg + k*(B1 + C1*cg),
-  // evaluated mod 2^32 and then reduced mod N (N divides 2^32).
+  // evaluated mod 2^32 and then reduced mod N (N divides 2^32).  Along each
+  // thread's sequence of outputs the exponent grows by a fixed step, so the
+  // twiddle is carried by complex multiplication and re-read from the table
+  // every kAnchor outputs (bounded rounding growth, few scattered lookups).
+  constexpr int kAnchor = 8;
   const uint32_t nmask = (uint32_t)a.nmask;
-  const uint32_t A1 = (uint32_t)(a.tw_mul * o1 * a.tw_a);
-  const uint32_t B1 = (uint32_t)(a.tw_mul * o1 * a.tw_b);
+  const long long od = o1 % a.tw_modo;  // the input digit this twiddle multiplies
+  const uint32_t A1 = (uint32_t)(a.tw_mul * od * a.tw_a);
+  const uint32_t B1 = (uint32_t)(a.tw_mul * od * a.tw_b);
   const uint32_t C1 = (uint32_t)(a.tw_mul * a.tw_c);
-  auto twiddled = [&](float2 v, uint32_t cg, uint32_t k) {
-    if (a.has_tw) {
-      float2 w = twiddle2(a, (A1 * cg + k * (B1 + C1 * cg)) & nmask);
-      if (INV) w.y = -w.y;
-      v = make_float2(v.x * w.x - v.y * w.y, v.x * w.y + v.y * w.x);
-    }
-    return make_float2(v.x * a.scale, v.y * a.scale);
+  const bool tw = a.has_tw != 0;
+  const float sc = a.scale;
+  auto cmul = [](float2 x, float2 y) { return make_float2(x.x * y.x - x.y * y.y, x.x * y.y + x.y * y.x); };
+  auto look = [&](uint32_t e) {
+    float2 w = twiddle2(a, e & nmask);
+    if (INV) w.y = -w.y;
+    return w;
   };
   if constexpr (KIND == 0) {
-    // column-wise, same thread mapping as the load
+    // column-wise, same thread mapping as the load: k = r0 + i*RSTEP
     if (colok) {
       const long long cg = c0 + cl;
-      const long long base = o2 * a.os_o2 + o1 * a.os_o1 + cg + (long long)r0 * a.os_k;
+      const long long base = obase + cg + (long long)r0 * a.os_k;
       float* __restrict__ qr = a.yr + base;
       float* __restrict__ qi = a.yi + base;
       const long long step = (long long)RSTEP * a.os_k;
       const float2* src = sm2 + cl * GM::PITCH;
+      const uint32_t de = B1 + C1 * (uint32_t)cg;
+      const uint32_t e0 = A1 * (uint32_t)cg + (uint32_t)r0 * de;
+      float2 w = make_float2(1.f, 0.f), d = w;
+      if (tw) d = look((uint32_t)RSTEP * de);
 #pragma unroll
       for (int i = 0; i < ITER; ++i) {
-        const int k = r0 + i * RSTEP;
-        const float2 v = twiddled(src[spad<S::SH>(k)], (uint32_t)cg, (uint32_t)k);
-        qr[i * step] = v.x;
-        qi[i * step] = v.y;
+        float2 v = src[spad<S::SH>(r0 + i * RSTEP)];
+        if (tw) {
+          w = (i % kAnchor == 0) ? look(e0 + (uint32_t)i * RSTEP * de) : cmul(w, d);
+          v = cmul(v, w);
+        }
+        qr[i * step] = v.x * sc;
+        qi[i * step] = v.y * sc;
       }
     }
   } else {
     // row-wise: consecutive threads take consecutive k of one column
-    float* __restrict__ qr0 = a.yr + o2 * a.os_o2 + o1 * a.os_o1;
-    float* __restrict__ qi0 = a.yi + o2 * a.os_o2 + o1 * a.os_o1;
+    float* __restrict__ qr0 = a.yr + obase;
+    float* __restrict__ qi0 = a.yi + obase;
+    if constexpr (THREADS <= L) {
+      constexpr int R = L / THREADS;  // k = q*THREADS + tid, columns c = 0..CT-1
 #pragma unroll
-    for (int i = 0; i < ITER; ++i) {
-      const int idx = i * THREADS + tid;
-      const int c = idx >> LOGL;
-      const int k = idx & (L - 1);
-      const long long cg = c0 + c;
-      if (cg < a.ncols) {
-        const float2 v = twiddled(sm2[c * GM::PITCH + spad<S::SH>(k)], (uint32_t)cg, (uint32_t)k);
-        const long long off = cg * a.os_c + k;
-        qr0[off] = v.x;
-        qi0[off] = v.y;
+      for (int q = 0; q < R; ++q) {
+        const int k = q * THREADS + tid;
+        const uint32_t mstep = A1 + C1 * (uint32_t)k;  // exponent step per column
+        float2 w = make_float2(1.f, 0.f), m = w;
+        if (tw) m = look(mstep);
+#pragma unroll
+        for (int c = 0; c < CT; ++c) {
+          const long long cg = c0 + c;
+          if (cg < a.ncols) {
+            float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
+            if (tw) {
+              w = (c % kAnchor == 0) ? look(A1 * (uint32_t)cg + (uint32_t)k * (B1 + C1 * (uint32_t)cg))
+                                     : cmul(w, m);
+              v = cmul(v, w);
+            }
+            const long long off = cg * a.os_c + k;
+            qr0[off] = v.x * sc;
+            qi0[off] = v.y * sc;
+          }
+        }
+      }
+    } else {
+      constexpr int CPI = THREADS / L;  // columns per iteration; k fixed per thread
+      const int k = tid % L;
+      const int cst = tid / L;
+      const uint32_t mstep = (uint32_t)CPI * (A1 + C1 * (uint32_t)k);
+      float2 w = make_float2(1.f, 0.f), m = w;
+      if (tw) m = look(mstep);
+#pragma unroll
+      for (int i = 0; i < ITER; ++i) {
+        const int c = i * CPI + cst;
+        const long long cg = c0 + c;
+        float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
+        if (tw) {
+          w = (i % kAnchor == 0) ? look(A1 * (uint32_t)cg + (uint32_t)k * (B1 + C1 * (uint32_t)cg)) : cmul(w, m);
+          v = cmul(v, w);
+        }
+        if (cg < a.ncols) {
+          const long long off = cg * a.os_c + k;
+          qr0[off] = v.x * sc;
+          qi0[off] = v.y * sc;
+        }
       }
     }
   }
@@ -149,8 +199,10 @@ static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
     if (e != cudaSuccess) return e;
   }
+  cudaError_t e0 = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e0 != cudaSuccess) return e0;
   const long long ncb = (a.ncols + GM::CT - 1) / GM::CT;
-  const long long tiles = ncb * a.O1 * a.O2;
+  const long long tiles = ncb * a.O1 * a.O2 * a.O3;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   kern<<<(unsigned)tiles, GM::THREADS, GM::smem, st>>>(a);

@@ -38,22 +38,25 @@ struct BlueArgs {
 cudaError_t launch_bluestein(int logm, int mode, bool inv, const BlueArgs& a, cudaStream_t st);
 
 // Column-tile FFT pass (colpass.cu).  Tile = CT neighbouring columns
-// c in [c0, c0+CT) of L-point transforms.  Point j of column c of outer block
-// (o2, o1) is read at x + o2*is_o2 + o1*is_o1 + c + j*is_j.  Output k goes to
-//   kind 0: y + o2*os_o2 + o1*os_o1 + c + k*os_k
-//   kind 1: y + o2*os_o2 + o1*os_o1 + c*os_c + k
-// after multiplication by W_N^e, e = tw_mul*(o1*(tw_a*c + tw_b*k) + tw_c*c*k)
-// mod N (two-level table: W_N^e = tw_hi[e >> tw_split] * tw_lo[e & mask]).
+// c in [c0, c0+CT) of L-point transforms, for outer block (o1, o2, o3).
+// Point j of column c is read at
+//   x + o1*is_o1 + o2*is_o2 + o3*is_o3 + c + j*is_j
+// and output k goes to
+//   kind 0: y + o1*os_o1 + o2*os_o2 + o3*os_o3 + c + k*os_k
+//   kind 1: y + o1*os_o1 + o2*os_o2 + o3*os_o3 + c*os_c + k
+// after multiplication by W_N^e,
+//   e = tw_mul*((o1 mod tw_modo)*(tw_a*c + tw_b*k) + tw_c*c*k)  (mod N),
+// with W_N^e = tw_hi[e >> tw_split] * tw_lo[e & (2^tw_split - 1)].
 struct ColArgs {
   const float* xr;
   const float* xi;
   float* yr;
   float* yi;
-  long long ncols, O1, O2;
-  long long is_o1, is_o2, is_j;
-  long long os_o1, os_o2, os_k, os_c;
+  long long ncols, O1, O2, O3;
+  long long is_o1, is_o2, is_o3, is_j;
+  long long os_o1, os_o2, os_o3, os_k, os_c;
   int has_tw;
-  long long tw_mul, tw_a, tw_b, tw_c;
+  long long tw_mul, tw_a, tw_b, tw_c, tw_modo;
   long long nmask;
   int tw_split;
   const float2* tw_hi;
