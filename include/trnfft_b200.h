@@ -146,6 +146,22 @@ TRNFFT_API int trnfft_exec_stft(trnfft_plan_t plan, const float* signal, int64_t
                                 int64_t hop, const float* window, int center, int pad_mode, int normalized,
                                 int onesided, int64_t frames, float* out_re, float* out_im, void* stream);
 
+/* Work-area bytes trnfft_complex_linear needs: the TF32 hi/lo split of x and
+ * W, 4*(M+N)*K floats.  -1 for negative sizes. */
+TRNFFT_API int64_t trnfft_complex_linear_work_bytes(int64_t M, int64_t N, int64_t K);
+
+/* Complex linear map y = x W^T (+ b) on planar complex operands:
+ * x (M x K), W (N x K, the nn.Linear weight layout), y (M x N), row-major,
+ * b (N) optional (both parts or neither).  Replaces ComplexLinear.forward
+ * (trnfft/nn.py:33-49) and trnfft.nki.dispatch.complex_linear
+ * (trnfft/nki/dispatch.py:91-102): two tcgen05 TF32 tensor-core GEMMs with
+ * the 3xTF32 split (hi*hi + hi*lo + lo*hi), float32 accuracy.  K must be a
+ * multiple of 4; all pointers 16-byte aligned; `work` holds
+ * trnfft_complex_linear_work_bytes(M, N, K) bytes. */
+TRNFFT_API int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, const float* wi,
+                                     const float* br, const float* bi, float* yr, float* yi, int64_t M,
+                                     int64_t N, int64_t K, void* work, int device, void* stream);
+
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex
  * transform of the real row and keeps the first n//2+1 bins. */

@@ -1,0 +1,68 @@
+"""GPU parity of the tcgen05 3xTF32 complex GEMM (ComplexLinear, complex_matmul)."""
+
+import numpy as np
+import pytest
+import torch
+
+import trnfft_b200 as trnfft
+from trnfft_b200 import ComplexTensor, _lib
+from trnfft_b200.nn import ComplexLinear
+from tests.helpers import TOL, cplx, cuda, host, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def test_linear_vs_reference_golden(golden):
+    g = golden("linear")
+    layer = ComplexLinear(96, 48).cuda()
+    with torch.no_grad():
+        layer.W_re.weight.copy_(cuda(g["w_re"]))
+        layer.W_im.weight.copy_(cuda(g["w_im"]))
+        layer.bias_re.copy_(cuda(g["b_re"]))
+        layer.bias_im.copy_(cuda(g["b_im"]))
+        y = layer(ComplexTensor(cuda(g["x_re"]), cuda(g["x_im"])))
+    assert rel_l2(cplx(y), g["y_re"] + 1j * g["y_im"]) < TOL
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 32), (300, 200, 128), (1, 7, 5), (1000, 513, 260), (2048, 1024, 1024)])
+def test_linear_vs_fp64(M, N, K):
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)) + 1j * rng.standard_normal((M, K))
+    w = (rng.uniform(-1, 1, (N, K)) + 1j * rng.uniform(-1, 1, (N, K))) / np.sqrt(K)
+    x = x.astype(np.complex64)
+    w = w.astype(np.complex64)
+    xr, xi = cuda(x.real), cuda(x.imag)
+    y = trnfft.nki.dispatch.complex_linear(ComplexTensor(xr, xi), cuda(w.real), cuda(w.imag))
+    ref = x.astype(np.complex128) @ w.astype(np.complex128).T
+    assert rel_l2(cplx(y), ref) < TOL
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+
+
+def test_complex_matmul_vs_reference_golden(golden):
+    g = golden("linear")
+    a = ComplexTensor(cuda(g["a_re"]), cuda(g["a_im"]))
+    b = ComplexTensor(cuda(g["b2_re"]), cuda(g["b2_im"]))
+    c = trnfft.complex_matmul(a, b)
+    assert rel_l2(cplx(c), g["c_re"] + 1j * g["c_im"]) < TOL
+    c2 = a @ b
+    assert rel_l2(cplx(c2), g["c_re"] + 1j * g["c_im"]) < TOL
+
+
+def test_linear_gradients_match_torch():
+    torch.manual_seed(0)
+    layer = ComplexLinear(64, 32).cuda()
+    xr = torch.randn(8, 64, device="cuda", requires_grad=True)
+    xi = torch.randn(8, 64, device="cuda", requires_grad=True)
+    y = layer(ComplexTensor(xr, xi))
+    (y.real ** 2 + y.imag ** 2).sum().backward()
+    wr = layer.W_re.weight.detach().clone().requires_grad_(True)
+    wi = layer.W_im.weight.detach().clone().requires_grad_(True)
+    zr = xr.detach().clone().requires_grad_(True)
+    zi = xi.detach().clone().requires_grad_(True)
+    re = zr @ wr.t() - zi @ wi.t()
+    im = zr @ wi.t() + zi @ wr.t()
+    (re ** 2 + im ** 2).sum().backward()
+    assert rel_l2(host(layer.W_re.weight.grad), host(wr.grad)) < 1e-5
+    assert rel_l2(host(layer.W_im.weight.grad), host(wi.grad)) < 1e-5
+    assert rel_l2(host(xr.grad), host(zr.grad)) < 1e-5

@@ -1,31 +1,107 @@
-"""Complex GEMM entry points used by complex_matmul and ComplexLinear.
+"""Complex GEMM entry points behind complex_matmul and ComplexLinear.
 
-Stage 1 (this file as first written): planar complex products composed from
-real device matmuls, the reference's pytorch formulation
-(trnfft/complex.py:142-150, trnfft/nn.py:44-48).  The tcgen05 3xTF32 kernel
-replaces these bodies.
+``complex_linear`` runs the library's tcgen05 tensor-core GEMM
+(trnfft_complex_linear: two TF32 GEMMs with the 3xTF32 split, float32
+accuracy).  ``complex_matmul`` (C = A @ B) maps onto the same kernel with
+W = B^T.  Backward passes use the analytic adjoints of
+trnfft/nki/autograd.py:125-159 evaluated with device matmuls, as the
+reference does for its kernels' backward.
 """
 
 from __future__ import annotations
 
 import torch
 
+from . import _lib
 from ._device import place
 from .complex import ComplexTensor
 
 
-def complex_matmul(a: ComplexTensor, b: ComplexTensor) -> ComplexTensor:
-    (ar, ai, br, bi), restore = place(a.real, a.imag, b.real, b.imag)
-    re = torch.matmul(ar, br) - torch.matmul(ai, bi)
-    im = torch.matmul(ar, bi) + torch.matmul(ai, br)
-    return ComplexTensor(restore(re), restore(im))
+def _pad_k(t: torch.Tensor, k4: int) -> torch.Tensor:
+    k = t.shape[-1]
+    if k == k4:
+        return t.contiguous()
+    return torch.nn.functional.pad(t, (0, k4 - k)).contiguous()
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+def linear_raw(xr, xi, wr, wi, br=None, bi=None):
+    """y = x W^T + b for 2-D planar complex x (M x K) and W (N x K) on CUDA."""
+    M, K = xr.shape
+    N = wr.shape[0]
+    k4 = (K + 3) // 4 * 4
+    xr, xi, wr, wi = (_aligned(_pad_k(t.float(), k4)) for t in (xr, xi, wr, wi))
+    if br is not None:
+        br = _aligned(br.float())
+        bi = _aligned(bi.float())
+    yr = torch.empty(M, N, dtype=torch.float32, device=xr.device)
+    yi = torch.empty_like(yr)
+    if M and N:
+        wb = _lib.load().trnfft_complex_linear_work_bytes(M, N, k4)
+        work = torch.empty(wb, dtype=torch.uint8, device=xr.device)
+        _lib.call("trnfft_complex_linear", _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(wr), _lib.ptr(wi),
+                  _lib.ptr(br), _lib.ptr(bi), _lib.ptr(yr), _lib.ptr(yi), M, N, k4, _lib.ptr(work),
+                  xr.device.index if xr.device.index is not None else torch.cuda.current_device(),
+                  _lib.stream_ptr(xr.device))
+    return yr, yi
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, xr, xi, wr, wi, br, bi):
+        ctx.save_for_backward(xr, xi, wr, wi)
+        ctx.has_bias = br is not None
+        return linear_raw(xr, xi, wr, wi, br, bi)
+
+    @staticmethod
+    def backward(ctx, gr, gi):
+        xr, xi, wr, wi = ctx.saved_tensors
+        # dX = dY conj(W); dW = dY^T conj(X) (trnfft/nki/autograd.py:147-159)
+        dxr = gr @ wr + gi @ wi
+        dxi = gi @ wr - gr @ wi
+        dwr = gr.t() @ xr + gi.t() @ xi
+        dwi = gi.t() @ xr - gr.t() @ xi
+        dbr = gr.sum(0) if ctx.has_bias else None
+        dbi = gi.sum(0) if ctx.has_bias else None
+        return dxr, dxi, dwr, dwi, dbr, dbi
 
 
 def complex_linear(x: ComplexTensor, w_re, w_im, b_re=None, b_im=None) -> ComplexTensor:
-    (xr, xi, wr, wi), restore = place(x.real, x.imag, w_re, w_im)
-    re = xr @ wr.t() - xi @ wi.t()
-    im = xr @ wi.t() + xi @ wr.t()
-    if b_re is not None:
-        re = re + b_re.to(re.device)
-        im = im + b_im.to(im.device)
-    return ComplexTensor(restore(re), restore(im))
+    if b_re is not None and b_im is None:
+        b_im = torch.zeros_like(b_re)
+    ts = [x.real, x.imag, w_re, w_im] + ([b_re, b_im] if b_re is not None else [])
+    dev_ts, restore = place(*ts)
+    xr, xi, wr, wi = dev_ts[:4]
+    br, bi = (dev_ts[4], dev_ts[5]) if b_re is not None else (None, None)
+    lead = xr.shape[:-1]
+    K = xr.shape[-1]
+    xr2, xi2 = xr.reshape(-1, K), xi.reshape(-1, K)
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (xr2, xi2, wr, wi, br, bi)):
+        yr, yi = _LinearFn.apply(xr2, xi2, wr, wi, br, bi)
+    else:
+        yr, yi = linear_raw(xr2, xi2, wr, wi, br, bi)
+    N = wr.shape[0]
+    return ComplexTensor(restore(yr.reshape(*lead, N)), restore(yi.reshape(*lead, N)))
+
+
+def complex_matmul(a: ComplexTensor, b: ComplexTensor) -> ComplexTensor:
+    """C = A @ B (trnfft/complex.py:142-150) as complex_linear with W = B^T."""
+    if a.real.dim() != 2 or b.real.dim() != 2:
+        # batched matmul: loop over the leading dims of broadcast-free inputs
+        if a.real.dim() == b.real.dim() and a.real.shape[:-2] == b.real.shape[:-2]:
+            lead = a.real.shape[:-2]
+            ar = a.real.reshape(-1, *a.real.shape[-2:])
+            ai = a.imag.reshape(-1, *a.imag.shape[-2:])
+            br_ = b.real.reshape(-1, *b.real.shape[-2:])
+            bi_ = b.imag.reshape(-1, *b.imag.shape[-2:])
+            outs = [complex_matmul(ComplexTensor(ar[i], ai[i]), ComplexTensor(br_[i], bi_[i]))
+                    for i in range(ar.shape[0])]
+            re = torch.stack([o.real for o in outs]).reshape(*lead, *outs[0].shape)
+            im = torch.stack([o.imag for o in outs]).reshape(*lead, *outs[0].shape)
+            return ComplexTensor(re, im)
+        raise ValueError("complex_matmul: expected 2-D operands or equal batch shapes")
+    return complex_linear(a, b.real.t().contiguous(), b.imag.t().contiguous())

@@ -82,6 +82,27 @@ struct StftArgs {
 
 cudaError_t launch_stft(int logn, const StftArgs& a, cudaStream_t st);
 
+// TF32 tensor-core GEMM with signed K-segments (gemm_tf32.cu):
+// C = sum_s (seg_neg[s] ? -1 : 1) * A[seg_a[s]] * B[seg_b[s]]^T (+ bias),
+// A_i: M x K (lda), B_i: N x K (ldb), C: M x N (ldc), row-major float32.
+#define GEMM_MAX_SEGS 6
+struct GemmArgs {
+  const float* A[4];
+  int na;
+  const float* B[4];
+  int nb;
+  int nseg;
+  int seg_a[GEMM_MAX_SEGS];
+  int seg_b[GEMM_MAX_SEGS];
+  int seg_neg[GEMM_MAX_SEGS];
+  float* C;
+  const float* bias;
+  long long M, N, K, lda, ldb, ldc;
+};
+
+cudaError_t launch_gemm_tf32(const GemmArgs& g, cudaStream_t st);
+cudaError_t launch_split_tf32(const float* x, float* hi, float* lo, long long n, float scale, cudaStream_t st);
+
 cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st);
 bool rows_c2c_tma_ok(int logn, const RowArgs& a);
 cudaError_t launch_rows_c2c_tma(int logn, bool inv, const RowArgs& a, cudaStream_t st);

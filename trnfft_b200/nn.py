@@ -40,8 +40,7 @@ class ComplexLinear(nn.Module):
     def forward(self, x: ComplexTensor) -> ComplexTensor:
         from .nki.dispatch import complex_linear
 
-        y = complex_linear(x, self.W_re.weight, self.W_im.weight, self.bias_re, self.bias_im)
-        return y
+        return complex_linear(x, self.W_re.weight, self.W_im.weight, self.bias_re, self.bias_im)
 
 
 class ComplexConv1d(nn.Module):
