@@ -65,6 +65,17 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_tensor_peak():
+    """Dense TF32 tensor peak: half the measured dense bf16 cuBLAS rate (TF32 issues at half
+    the bf16 rate on B200, 1.1 vs 2.25 PFLOP/s nominal)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return round(d["bf16_tflops"] / 2.0, 1), "measured bf16 / 2"
+    return round(1590.0 / 2.0, 1), "fallback bf16 / 2"
+
+
 def profiled_traffic(kernel_key):
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -420,7 +431,77 @@ class Fft2(Workload):
         return time.perf_counter() - t0, 2 * c2c_flops(s, s)
 
 
+class LinearWL(Workload):
+    """BASELINE configs[1](b): ComplexLinear 4096 -> 4096 on a 16384 x 4096 complex input."""
+
+    metric = "ComplexLinear GFLOP/s (8*M*N*K complex flops)"
+
+    def __init__(self, M=16384, N=4096, K=4096):
+        self.M, self.N, self.K = M, N, K
+        self.name = f"ComplexLinear {K}->{N} on a {M}x{K} complex fp32 input, 3xTF32 tcgen05 (configs[1]b)"
+        self.work = 8.0 * M * N * K
+        self.dom_bytes = None
+        self.dominant = "k_gemm_tf32 (two launches of six TF32 segments each)"
+        self.bound = "tensor"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+        from trnfft_b200 import ComplexTensor
+        from trnfft_b200.nn import ComplexLinear
+
+        torch.manual_seed(77)
+        self.layer = ComplexLinear(self.K, self.N, bias=True).to(dev)
+        self.xr = torch.randn(self.M, self.K, device=dev, generator=g)
+        self.xi = torch.randn(self.M, self.K, device=dev, generator=g)
+        x = ComplexTensor(self.xr, self.xi)
+        torch.set_grad_enabled(False)
+        self.step = lambda: self.layer(x)
+        self.launches = {"linear": self.step}
+        self.launches_per_step = 6  # 4 split kernels + 2 GEMMs
+        self.inputs = [self.xr, self.xi]
+        self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(self.layer(ComplexTensor(ts[0], ts[1])))
+
+    def check(self, out):
+        w_r, w_i = self.layer.W_re.weight, self.layer.W_im.weight
+        xr, xi = self.xr[:256].double(), self.xi[:256].double()
+        ref_r = xr @ w_r.double().t() - xi @ w_i.double().t()
+        ref_i = xr @ w_i.double().t() + xi @ w_r.double().t()
+        return rel_err(torch.complex(out.real[:256].double(), out.imag[:256].double()), torch.complex(ref_r, ref_i))
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        rng = np.random.default_rng(0)
+        r = max(16, rows // 4)
+        xr = rng.standard_normal((r, self.K)).astype(np.float32)
+        xi = rng.standard_normal((r, self.K)).astype(np.float32)
+        wr = rng.uniform(-1, 1, (self.N, self.K)).astype(np.float32) / 64
+        wi = rng.uniform(-1, 1, (self.N, self.K)).astype(np.float32) / 64
+        t0 = time.perf_counter()
+        O.complex_linear(xr, xi, wr, wi)
+        return time.perf_counter() - t0, 8.0 * r * self.N * self.K
+
+
+class SmallNGemm(SmallN):
+    """configs[1](a) on the DFT-as-GEMM tensor-core path."""
+
+    def __init__(self):
+        super().__init__()
+        self.name = "small-N batched C2C FFT as DFT-GEMM (tcgen05 3xTF32), N=64,128,256, batch=262144 (configs[1]a)"
+        self.dominant = "k_gemm_tf32 DFT-GEMM, N=256"
+        self.bound = "tensor"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+
+        trnfft.set_small_n_algorithm("gemm")
+        super().setup(dev, g)
+        self.tensor_flops = sum(3 * 8.0 * self.batch * n * n for n in (256,))
+
+
 WORKLOADS = {
+    "linear": LinearWL,
+    "smalln_gemm": SmallNGemm,
     "c2c1024": lambda: C2CRoundTrip(N, BATCH, "BASELINE configs[0]"),
     "smalln": SmallN,
     "stft": Stft,
@@ -583,7 +664,14 @@ def run_ours(args, world, rank, local):
         return
     peak, peak_kind = measured_peaks()
     avg_launch = sum(launch_ms) / len(launch_ms)
-    achieved = wl.dom_bytes / (avg_launch / 1e3) / 1e9
+    if getattr(wl, "bound", "hbm") == "tensor":
+        tf = getattr(wl, "tensor_flops", None) or 3.0 * wl.work  # 3xTF32: three TF32 products per flop
+        achieved_t = tf / (avg_launch / 1e3) / 1e12
+        tpeak, tkind = measured_tensor_peak()
+        roof = {"bound": "tensor", "achieved": round(achieved_t, 2), "peak": tpeak, "unit": "TFLOP/s",
+                "frac": round(achieved_t / tpeak, 4), "peak_source": tkind, "traffic": profiled_traffic(args.workload),
+                "kernel": wl.dominant, "tensor_flops_per_launch": tf, "avg_launch_ms": round(avg_launch, 5)}
+    achieved = (wl.dom_bytes or 1.0) / (avg_launch / 1e3) / 1e9
     out = {
         "metric": wl.metric, "value": round(scale_value(value, wl.unit), 3), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -591,7 +679,8 @@ def run_ours(args, world, rank, local):
         "data": "synthetic",
         "config": {"workload": wl.name, "parallelism": f"batch-sharded x{world}" if world > 1 else "1 GPU",
                    "l2": "flushed before every timed step (256 MiB read sweep)"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+        "roofline": roof if getattr(wl, "bound", "hbm") == "tensor" else
+                    {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                      "traffic": profiled_traffic(args.workload), "kernel": wl.dominant,
                      "algorithmic_bytes_per_launch": wl.dom_bytes, "avg_launch_ms": round(avg_launch, 5)},

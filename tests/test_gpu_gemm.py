@@ -66,3 +66,30 @@ def test_linear_gradients_match_torch():
     assert rel_l2(host(layer.W_re.weight.grad), host(wr.grad)) < 1e-5
     assert rel_l2(host(layer.W_im.weight.grad), host(wi.grad)) < 1e-5
     assert rel_l2(host(xr.grad), host(zr.grad)) < 1e-5
+
+
+@pytest.mark.parametrize("n", [8, 64, 128, 256])
+def test_dft_as_gemm_vs_reference_golden(golden, n):
+    """Small-n transforms on the tensor-core DFT-GEMM path (the reference's
+    NKI path for n <= 256, trnfft/fft_core.py:221-251)."""
+    g = golden("pow2_c2c")
+    trnfft.set_small_n_algorithm("gemm")
+    try:
+        x = ComplexTensor(cuda(g[f"x_re_{n}"]), cuda(g[f"x_im_{n}"]))
+        y = trnfft.fft(x)
+        z = trnfft.ifft(x)
+    finally:
+        trnfft.set_small_n_algorithm("stockham")
+    assert rel_l2(cplx(y), g[f"fft_re_{n}"] + 1j * g[f"fft_im_{n}"]) < TOL
+    assert rel_l2(cplx(z), g[f"ifft_re_{n}"] + 1j * g[f"ifft_im_{n}"]) < TOL
+
+
+def test_dft_as_gemm_large_batch_vs_fp64():
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((4096, 256)) + 1j * rng.standard_normal((4096, 256))).astype(np.complex64)
+    trnfft.set_small_n_algorithm("gemm")
+    try:
+        y = trnfft.fft(ComplexTensor(cuda(x.real), cuda(x.imag)))
+    finally:
+        trnfft.set_small_n_algorithm("stockham")
+    assert rel_l2(cplx(y), np.fft.fft(x.astype(np.complex128))) < 2e-6

@@ -29,7 +29,7 @@ from .api import (
 )
 from .complex import ComplexTensor, complex_matmul
 from .nki import HAS_NKI, get_backend, set_backend
-from .plan import FFTPlan, clear_plan_cache, create_plan
+from .plan import FFTPlan, clear_plan_cache, create_plan, get_small_n_algorithm, set_small_n_algorithm
 from .precision import get_precision, set_precision
 
 
@@ -42,7 +42,7 @@ __all__ = [
     "fft", "ifft", "rfft", "hfft", "ihfft", "irfft", "fft2", "fftn", "ifftn", "rfft2", "irfft2",
     "rfftn", "irfftn", "stft", "istft",
     "ComplexTensor", "complex_matmul",
-    "create_plan", "clear_plan_cache", "FFTPlan",
+    "create_plan", "clear_plan_cache", "FFTPlan", "set_small_n_algorithm", "get_small_n_algorithm",
     "HAS_NKI", "set_backend", "get_backend",
     "set_precision", "set_ozaki_product_precision_verified", "get_precision",
 ]

@@ -35,10 +35,42 @@ def _check(t: torch.Tensor, what: str) -> None:
 # ---------------------------------------------------------------------------
 
 
+_dft_cache: dict = {}
+
+
+def _dft_matrix(n: int, inverse: bool, device: torch.device):
+    """n x n DFT matrix exp(-+2 pi i j k / n) (/n for the inverse), float32 planes, cached."""
+    key = (n, inverse, device)
+    m = _dft_cache.get(key)
+    if m is None:
+        j = torch.arange(n, dtype=torch.int64)
+        e = (j[:, None] * j[None, :]) % n
+        ang = (2.0 * torch.pi / n) * e.to(torch.float64) * (1.0 if inverse else -1.0)
+        sc = (1.0 / n) if inverse else 1.0
+        m = ((torch.cos(ang) * sc).float().to(device).contiguous(), (torch.sin(ang) * sc).float().to(device).contiguous())
+        _dft_cache[key] = m
+    return m
+
+
+def dft_gemm_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool):
+    """Power-of-two n <= 256 as X = x F on the tcgen05 3xTF32 GEMM (F symmetric, so W = F)."""
+    from . import _gemm
+
+    n = xr.shape[-1]
+    shape = xr.shape
+    fr, fi = _dft_matrix(n, inverse, xr.device)
+    yr, yi = _gemm.linear_raw(xr.reshape(-1, n), xi.reshape(-1, n), fr, fi)
+    return yr.reshape(shape), yi.reshape(shape)
+
+
 def c2c_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool) -> tuple[torch.Tensor, torch.Tensor]:
     _check(xr, "real part")
     _check(xi, "imaginary part")
     n = xr.shape[-1]
+    from .plan import DFT_GEMM_MAX_N, get_small_n_algorithm
+
+    if get_small_n_algorithm() == "gemm" and 4 <= n <= DFT_GEMM_MAX_N and (n & (n - 1)) == 0:
+        return dft_gemm_raw(xr, xi, inverse)
     shape = xr.shape
     a = _flat(xr, n)
     b = _flat(xi, n)

@@ -55,3 +55,26 @@ def clear_plan_cache():
     from . import _lib
 
     _lib.clear_device_plans()
+
+
+# Power-of-two transforms with n <= 256 can run either on the Stockham kernel
+# (memory bound, one HBM pass) or as a DFT-as-GEMM on the tcgen05 tensor
+# cores (X = x F with the n x n DFT matrix F, 3xTF32 for float32 accuracy),
+# the B200 counterpart of the reference's NKI DFT-GEMM path for n <= 256
+# (trnfft/fft_core.py:138, 221-251).  "stockham" is the default because it
+# measured faster on B200 (the GEMM does O(n) more arithmetic per point).
+_SMALL_N_MODES = ("stockham", "gemm")
+_small_n_algorithm = "stockham"
+DFT_GEMM_MAX_N = 256
+
+
+def set_small_n_algorithm(mode: str) -> None:
+    """Select the kernel for power-of-two n <= 256: "stockham" or "gemm"."""
+    global _small_n_algorithm
+    if mode not in _SMALL_N_MODES:
+        raise ValueError(f"small-n algorithm must be one of {_SMALL_N_MODES}; got {mode!r}")
+    _small_n_algorithm = mode
+
+
+def get_small_n_algorithm() -> str:
+    return _small_n_algorithm
