@@ -513,6 +513,19 @@ WORKLOADS = {
 }
 
 
+def make_workload(args):
+    """Build the workload; --size shrinks the size-parametrised ones for profiling runs
+    (large: log2 N, fft2: side, linear: M rows)."""
+    if args.size:
+        if args.workload == "large":
+            return Large(args.size)
+        if args.workload == "fft2":
+            return Fft2(args.size)
+        if args.workload == "linear":
+            return LinearWL(M=args.size)
+    return WORKLOADS[args.workload]()
+
+
 def cpu_rate(wl, threads, budget_s, rows=256):
     wl.cpu_sample(threads, max(8, rows // 8))  # warm-up
     t_total, w_total, reps = 0.0, 0.0, 0
@@ -541,7 +554,7 @@ def cpu_baseline(wl, budget_s):
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    wl = WORKLOADS[args.workload]()
+    wl = make_workload(args)
     threads = os.cpu_count() or 1
     for _ in range(args.warmup):
         wl.cpu_sample(threads, 64)
@@ -575,7 +588,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    wl = WORKLOADS[args.workload]()
+    wl = make_workload(args)
     wl.setup(dev, g)
     flush = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
     flush_out = torch.empty(1, dtype=torch.float32, device=dev)
@@ -706,6 +719,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2c1024")
+    ap.add_argument("--size", type=int, default=0, help="smaller case for profiling (large/fft2/linear)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:
