@@ -1,0 +1,185 @@
+"""Multi-GPU transforms: one process per GPU, torch.distributed (NCCL) for the exchanges.
+
+* Batched transforms shard by batch (``shard_rows`` / ``batch_sharded_fft``): every rank
+  transforms its own rows, no communication -- the reference's batch split
+  (trnfft/nki/multicore.py:222-260) with one process per device.
+* A single large 1-D transform (``fft_distributed``) runs the four-step algorithm of
+  trnfft/nki/multicore.py:151-219 across ranks.  With N = N1*N2 and n = n1*N2 + n2,
+      X[k1 + N1*k2] = sum_n2 W_N^{n2 k1} W_N2^{n2 k2} sum_n1 x[n1 N2 + n2] W_N1^{n1 k1}.
+  Rank p holds the contiguous input chunk x[p N/P : (p+1) N/P] (rows n1 of block p).
+  1. all-to-all: rank p receives every row's columns n2 of block p   -> [N1][N2/P]
+  2. length-N1 transforms down the columns (strided-axis kernel, no transposes)
+  3. twiddle W_N^{n2 k1} (exponent reduced exactly in integers)
+  4. all-to-all: rank p receives rows k1 of block p                 -> [N1/P][N2]
+  5. length-N2 transforms along the rows
+  The result is X[k1 + N1*k2] for k1 in block p ("transposed" distribution).  With
+  ``natural_order=True`` a third all-to-all returns the contiguous chunk
+  X[p N/P : (p+1) N/P] to rank p.
+* ``fft2_distributed``: rows of a 2-D field sharded across ranks; row transforms, one
+  all-to-all transpose, column transforms (output in column-block layout, or row layout again
+  with ``natural_order=True``).
+
+The exchanges only move tensors, so they work with any process-group backend; the transforms
+are the library's CUDA kernels.  ``_four_step`` takes the transforms as arguments so the
+exchange logic can be checked with CPU (gloo) ranks and a reference transform.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from .complex import ComplexTensor
+
+
+def shard_rows(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous row range [lo, hi) of rank `rank` when `total` rows are split over `world`."""
+    base, extra = divmod(total, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def batch_sharded_fft(x_local: ComplexTensor, inverse: bool = False) -> ComplexTensor:
+    """Transform this rank's shard of a batch (no communication)."""
+    from .fft_core import fft_core
+
+    return fft_core(x_local, inverse=inverse)
+
+
+def _world(group):
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _a2a(t: torch.Tensor, group) -> torch.Tensor:
+    """all_to_all on equal contiguous chunks of the leading dimension."""
+    t = t.contiguous()
+    out = torch.empty(t.shape, dtype=t.dtype, device=t.device)
+    dist.all_to_all_single(out, t, group=group)
+    return out
+
+
+def _split_n(n: int) -> tuple[int, int]:
+    l1 = int(math.log2(n)) // 2
+    return 1 << l1, n >> l1
+
+
+def _twiddle(yr, yi, n, col0, inverse):
+    """Multiply Y[k1][c] by W_N^{(col0 + c) k1} (exponent reduced mod N in int64)."""
+    n1, cols = yr.shape
+    k1 = torch.arange(n1, device=yr.device, dtype=torch.int64).unsqueeze(1)
+    c = torch.arange(cols, device=yr.device, dtype=torch.int64).unsqueeze(0) + col0
+    e = (k1 * c) % n
+    ang = e.to(torch.float64) * ((2.0 if inverse else -2.0) * math.pi / n)
+    wr = torch.cos(ang).to(yr.dtype)
+    wi = torch.sin(ang).to(yr.dtype)
+    return yr * wr - yi * wi, yr * wi + yi * wr
+
+
+def _four_step(xr, xi, n, group, inverse, natural_order, col_fft, row_fft, columns_in=False):
+    """Exchange skeleton of the distributed four-step FFT (see the module docstring).
+
+    col_fft(re, im, inverse) transforms along dim 0 of [N1][C]; row_fft along dim 1 of [R][N2].
+    With columns_in, rank p already holds the column block [N1][N2/P] (x[n1 N2 + n2] for n2
+    in block p) and step 1's exchange is skipped: one all-to-all per transform.
+    """
+    P, p = _world(group)
+    N1, N2 = _split_n(n)
+    if N1 % P or N2 % P:
+        raise ValueError(f"N={n} (= {N1} x {N2}) must split evenly over {P} ranks")
+    r1, c2 = N1 // P, N2 // P
+    if columns_in:
+        ar = xr.reshape(N1, c2)
+        ai = xi.reshape(N1, c2)
+    else:
+        # 1. rows n1 of block p -> columns n2 of block p: pack [r1][P][c2] -> [P][r1][c2]
+        sr = xr.reshape(r1, P, c2).transpose(0, 1)
+        si = xi.reshape(r1, P, c2).transpose(0, 1)
+        ar = _a2a(sr, group).reshape(N1, c2)  # sources q in n1 order: [q][r1][c2] = [N1][c2]
+        ai = _a2a(si, group).reshape(N1, c2)
+    # 2. transforms over n1 (down the columns)
+    yr, yi = col_fft(ar, ai, inverse)
+    # 3. twiddle W_N^{n2 k1}, n2 = p*c2 + c
+    yr, yi = _twiddle(yr, yi, n, p * c2, inverse)
+    # (for the inverse, 1/N comes from the two inverse transforms: 1/N1 and 1/N2)
+    # 4. rows k1 of block q go to rank q: chunks are contiguous row blocks of [N1][c2]
+    br = _a2a(yr, group).reshape(P, r1, c2).transpose(0, 1).reshape(r1, N2)
+    bi = _a2a(yi, group).reshape(P, r1, c2).transpose(0, 1).reshape(r1, N2)
+    # 5. transforms over n2 along the rows: Z[k1 local][k2] = X[k1 + N1 k2]
+    zr, zi = row_fft(br.contiguous(), bi.contiguous(), inverse)
+    if not natural_order:
+        return zr, zi
+    # natural order: rank q owns k in [q N/P, (q+1) N/P) <=> k2 in block q (k = k1 + N1 k2)
+    tr = zr.reshape(r1, P, c2).transpose(0, 1)  # [dest q][k1 local][k2 local]
+    ti = zi.reshape(r1, P, c2).transpose(0, 1)
+    gr = _a2a(tr, group).reshape(P, r1, c2)  # [src s][k1 local of s][k2 local]
+    gi = _a2a(ti, group).reshape(P, r1, c2)
+    # local element (k2 local, k1 = s*r1 + j): index k - p*N/P = k1 + N1*k2_local
+    return (gr.permute(2, 0, 1).reshape(c2 * N1).contiguous(),
+            gi.permute(2, 0, 1).reshape(c2 * N1).contiguous())
+
+
+def _cuda_col_fft(re, im, inverse):
+    from . import _ops
+
+    return _ops.c2c_axis_raw(re.contiguous(), im.contiguous(), 0, inverse)
+
+
+def _cuda_row_fft(re, im, inverse):
+    from . import _ops
+
+    return _ops.c2c_raw(re, im, inverse)
+
+
+def column_block(x_full_re: torch.Tensor, x_full_im: torch.Tensor, n: int, world: int, rank: int):
+    """This rank's column block [N1][N2/P] of a full length-n signal (for columns_in=True)."""
+    N1, N2 = _split_n(n)
+    c2 = N2 // world
+    sl = slice(rank * c2, (rank + 1) * c2)
+    return (x_full_re.reshape(N1, N2)[:, sl].contiguous(), x_full_im.reshape(N1, N2)[:, sl].contiguous())
+
+
+def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natural_order: bool = True,
+                    group=None, columns_in: bool = False) -> ComplexTensor:
+    """Distributed 1-D FFT of length n = 2^k.
+
+    Rank p passes its contiguous chunk of n/P points, or with ``columns_in`` its column block
+    [N1][N2/P] (``column_block``), which saves one all-to-all.  The result is the contiguous
+    chunk of X (``natural_order``) or X[k1 + N1*k2] for k1 in block p stored [k1][k2].
+    """
+    P, _ = _world(group)
+    if n & (n - 1) or x_local.real.numel() * P != n:
+        raise ValueError("fft_distributed: n must be a power of two and every rank must hold n/P points")
+    xr = x_local.real.reshape(-1).float().contiguous()
+    xi = x_local.imag.reshape(-1).float().contiguous()
+    zr, zi = _four_step(xr, xi, n, group, inverse, natural_order, _cuda_col_fft, _cuda_row_fft, columns_in)
+    return ComplexTensor(zr, zi)
+
+
+def _fft2_exchange(xr, xi, group, inverse, natural_order, row_fft, col_fft):
+    """Exchange skeleton of fft2 over row-sharded [H/P][W] blocks."""
+    P, _ = _world(group)
+    hr, w = xr.shape
+    h = hr * P
+    if w % P:
+        raise ValueError("fft2_distributed: the width must split evenly over the ranks")
+    yr, yi = row_fft(xr, xi, inverse)
+    cw = w // P
+    # transpose blocks: rank q gets columns of block q from every row block -> [H][W/P]
+    ar = _a2a(yr.reshape(hr, P, cw).transpose(0, 1), group).reshape(h, cw)
+    ai = _a2a(yi.reshape(hr, P, cw).transpose(0, 1), group).reshape(h, cw)
+    zr, zi = col_fft(ar, ai, inverse)
+    if not natural_order:
+        return zr, zi
+    br = _a2a(zr.reshape(P, hr, cw), group)  # [src q (column block q)][hr][cw]
+    bi = _a2a(zi.reshape(P, hr, cw), group)
+    return br.permute(1, 0, 2).reshape(hr, w).contiguous(), bi.permute(1, 0, 2).reshape(hr, w).contiguous()
+
+
+def fft2_distributed(x_local: ComplexTensor, inverse: bool = False, natural_order: bool = True,
+                     group=None) -> ComplexTensor:
+    """fft2 of an [H][W] field whose rows are split evenly over the ranks ([H/P][W] each)."""
+    zr, zi = _fft2_exchange(x_local.real.float().contiguous(), x_local.imag.float().contiguous(), group,
+                            inverse, natural_order, _cuda_row_fft, _cuda_col_fft)
+    return ComplexTensor(zr, zi)
