@@ -355,6 +355,8 @@ class Stft(Workload):
 
 
 class Large(Workload):
+    metric = "single large C2C FFT GFLOP/s (5N*log2N)"
+
     """BASELINE configs[4]: one N = 2^30 complex forward FFT.
 
     One GPU: four column-tile passes.  N GPUs (torch.distributed.run): the four-step FFT of
@@ -429,6 +431,8 @@ class Large(Workload):
 
 
 class Fft2(Workload):
+    metric = "fft2 GFLOP/s (5N*log2N per row and column transform)"
+
     """BASELINE configs[4] second part: fft2 of a 16384 x 16384 complex field (1 GPU)."""
 
     def __init__(self, side=16384):

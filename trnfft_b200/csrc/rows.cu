@@ -23,21 +23,21 @@ namespace tfb {
 
 constexpr int kRowThreads = 256;
 
-template <int LOGN, int LOGE>
+template <int LOGN, int LOGE, int THR = kRowThreads>
 struct RowGeom {
   using S = Sched<LOGN, LOGE>;
-  static_assert(S::T <= kRowThreads && kRowThreads % S::T == 0,
-                "one transform must fit in one block of kRowThreads threads");
-  static constexpr int G = kRowThreads / S::T;  // transforms per block
+  static_assert(S::T <= THR && THR % S::T == 0, "one transform must fit in one block");
+  static constexpr int THREADS = THR;
+  static constexpr int G = THR / S::T;  // transforms per block
   static constexpr int NP = S::NP;
   static constexpr size_t smem = (size_t)G * NP * sizeof(float2);
 };
 
 // ----------------------------------------------------------------------------
-template <int LOGN, int LOGE, bool INV, int MINB = 1>
-__global__ void __launch_bounds__(kRowThreads, MINB) k_c2c(RowArgs a) {
+template <int LOGN, int LOGE, bool INV, int MINB = 1, int THR = kRowThreads>
+__global__ void __launch_bounds__(THR, MINB) k_c2c(RowArgs a) {
   using S = Sched<LOGN, LOGE>;
-  using GM = RowGeom<LOGN, LOGE>;
+  using GM = RowGeom<LOGN, LOGE, THR>;
   extern __shared__ float sm[];
   const int g = threadIdx.x / S::T;
   const int j = threadIdx.x % S::T;
@@ -191,32 +191,34 @@ __global__ void __launch_bounds__(kRowThreads) k_c2r(RowArgs a) {
 // Row-kernel tuning variants (values per thread E = 2^LOGE, min resident
 // blocks per SM).  Variant 0 is the default; the others are selectable with
 // the environment variable TRNFFT_B200_ROW_VARIANT for measurement.
-template <int LOGE_, int MINB_>
+template <int LOGE_, int MINB_, int THR_ = kRowThreads>
 struct RowVar {
   static constexpr int LOGE = LOGE_;
   static constexpr int MINB = MINB_;
+  static constexpr int THR = THR_;
 };
 
 template <int LOGN, bool INV, class V>
 static cudaError_t launch_c2c_v(const RowArgs& a, cudaStream_t st) {
   constexpr int LE = V::LOGE;
-  using GM = RowGeom<LOGN, LE>;
-  auto kern = k_c2c<LOGN, LE, INV, V::MINB>;
+  using GM = RowGeom<LOGN, LE, V::THR>;
+  auto kern = k_c2c<LOGN, LE, INV, V::MINB, V::THR>;
   const size_t smem = (Sched<LOGN, LE>::P == 1) ? 0 : GM::smem;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   const long long blocks = (a.batch + GM::G - 1) / GM::G;
-  kern<<<(unsigned)blocks, kRowThreads, smem, st>>>(a);
+  kern<<<(unsigned)blocks, V::THR, smem, st>>>(a);
   return cudaGetLastError();
 }
 
-// Measured defaults (B200, batch of 8M complex values, L2 flushed): radix-32
-// passes for N = 1024, three resident blocks per SM for N >= 2048.
+// Measured defaults (B200, batches of 8M complex values, L2 flushed before each
+// launch): 128-thread blocks everywhere from N = 256; radix-32 passes with four
+// resident blocks per SM for N = 512, 1024, 4096; radix-16 with six for 256, 2048.
 template <int LOGN>
 constexpr int default_row_variant() {
-  return LOGN == 10 ? 2 : (LOGN >= 11 ? 1 : 0);
+  return (LOGN == 8 || LOGN == 11) ? 10 : ((LOGN == 9 || LOGN == 10 || LOGN == 12) ? 8 : 0);
 }
 
 template <int LOGN, bool INV>
@@ -228,6 +230,29 @@ static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st, int variant) 
       case 2: return launch_c2c_v<LOGN, INV, RowVar<5, 1>>(a, st);
       case 3: return launch_c2c_v<LOGN, INV, RowVar<5, 2>>(a, st);
       case 5: return launch_c2c_v<LOGN, INV, RowVar<4, 2>>(a, st);
+      case 6: return launch_c2c_v<LOGN, INV, RowVar<5, 3>>(a, st);
+      case 7: return launch_c2c_v<LOGN, INV, RowVar<5, 4>>(a, st);
+      case 8:
+        if constexpr (LOGN <= 12 && (1 << LOGN) / 32 <= 128) return launch_c2c_v<LOGN, INV, RowVar<5, 4, 128>>(a, st);
+        break;
+      case 9:
+        if constexpr ((1 << LOGN) / 32 <= 128) return launch_c2c_v<LOGN, INV, RowVar<5, 6, 128>>(a, st);
+        break;
+      case 10:
+        if constexpr ((1 << LOGN) / 16 <= 128) return launch_c2c_v<LOGN, INV, RowVar<4, 6, 128>>(a, st);
+        break;
+      case 11:
+        if constexpr ((1 << LOGN) / 32 <= 64) return launch_c2c_v<LOGN, INV, RowVar<5, 8, 64>>(a, st);
+        break;
+      case 12:
+        if constexpr ((1 << LOGN) / 16 <= 128) return launch_c2c_v<LOGN, INV, RowVar<4, 8, 128>>(a, st);
+        break;
+      case 13:
+        if constexpr ((1 << LOGN) / 32 <= 128) return launch_c2c_v<LOGN, INV, RowVar<5, 5, 128>>(a, st);
+        break;
+      case 14:
+        if constexpr ((1 << LOGN) / 16 <= 64) return launch_c2c_v<LOGN, INV, RowVar<4, 10, 64>>(a, st);
+        break;
       default: break;
     }
   }
