@@ -22,15 +22,18 @@ namespace tfb {
 
 template <int LOGM>
 struct BlueLogE {
-  // values per thread: E = 16 up to m = 4096, E = 32 above (<= 512 threads)
-  static constexpr int v = LOGM <= 12 ? 4 : 5;
+  // 16 values per thread (radix-16 passes) up to m = 4096, where they beat the
+  // radix-32 variant (~250 registers, one block per SM) measured on B200
+  static constexpr int v = LOGM >= 13 ? 5 : 4;  // m >= 8192: radix-32 (measured faster there)
 };
 
 template <int LOGM>
 struct BlueGeom {
   static constexpr int LE = BlueLogE<LOGM>::v;
   using S = Sched<LOGM, LE>;
-  static constexpr int THREADS = S::T > 256 ? S::T : 256;
+  static constexpr int THREADS = S::T > 128 ? S::T : 128;
+  // <= 128 registers per thread for the radix-16 kernels; the radix-32 ones keep all they need
+  static constexpr int MINB = (LE == 5 || THREADS >= 512) ? 1 : 512 / THREADS;
   static constexpr int G = THREADS / S::T;
   static constexpr int MP = S::NP;
   static constexpr size_t smem = (size_t)G * MP * sizeof(float2);
@@ -38,7 +41,7 @@ struct BlueGeom {
 
 // MODE 0: C2C, MODE 1: R2C (real rows -> n/2+1 bins), MODE 2: C2R (n/2+1 bins -> real rows)
 template <int LOGM, bool INV, int MODE>
-__global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS) k_bluestein(BlueArgs a) {
+__global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS, BlueGeom<LOGM>::MINB) k_bluestein(BlueArgs a) {
   using GM = BlueGeom<LOGM>;
   constexpr int LE = GM::LE;
   using S = Sched<LOGM, LE>;
