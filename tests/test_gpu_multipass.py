@@ -137,3 +137,24 @@ def test_axis_autograd_matches_torch():
     (z.real * 3 + z.imag ** 2).sum().backward()
     assert rel_l2(host(xr.grad), host(zr.grad)) < 1e-5
     assert rel_l2(host(xi.grad), host(zi.grad)) < 1e-5
+
+
+@pytest.mark.parametrize("n1,cols,col0,big", [(512, 64, 192, 1 << 16), (4096, 32, 96, 1 << 20), (32768, 16, 16384, 1 << 30)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_axis_with_fused_four_step_twiddle(n1, cols, col0, big, inverse):
+    """trnfft_exec_c2c_axis_tw == column FFT followed by W_big^{(col0 + c) k} (fp64 reference)."""
+    rng = np.random.default_rng(n1 + cols)
+    x = (rng.standard_normal((n1, cols)) + 1j * rng.standard_normal((n1, cols))).astype(np.complex64)
+    xr, xi = cuda(x.real), cuda(x.imag)
+    yr, yi = torch.empty_like(xr), torch.empty_like(xi)
+    plan = _lib.device_plan(n1, xr.device)
+    twp = _lib.device_plan(big, xr.device)
+    _lib.call("trnfft_exec_c2c_axis_tw", plan.handle, twp.handle, _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(yr),
+              _lib.ptr(yi), 1, cols, int(inverse), col0, _lib.stream_ptr(xr.device))
+    xd = x.astype(np.complex128)
+    f = np.fft.ifft(xd, axis=0) if inverse else np.fft.fft(xd, axis=0)
+    k = np.arange(n1)[:, None]
+    c = np.arange(cols)[None, :] + col0
+    e = (k * c) % big
+    w = np.exp((2j if inverse else -2j) * np.pi * e / big)
+    assert rel_l2(host(yr) + 1j * host(yi), f * w) < 2e-6

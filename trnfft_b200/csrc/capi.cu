@@ -238,8 +238,24 @@ static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, c
 }
 
 // Transforms along the middle axis of an [outer][n][inner] array, inner > 1.
+// tw (optional): after the transform, output (o, K, s) is multiplied by
+// W_{tw->n}^{(coff + s) * K} using tw's tables (the four-step inter-pass twiddle).
 static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr, float* yi,
-                            int64_t outer, int64_t inner, bool inv, cudaStream_t st) {
+                            int64_t outer, int64_t inner, bool inv, cudaStream_t st,
+                            const trnfft_plan_s* tw = nullptr, int64_t coff = 0) {
+  auto extra_tw = [&](ColArgs& c, long long tw_c, long long tw_a) {
+    c.has_tw = 1;
+    c.nmask = tw->n - 1;
+    c.tw_split = tw->tw_split;
+    c.tw_hi = tw->tw_hi;
+    c.tw_lo = tw->tw_lo;
+    c.tw_mul = 1;
+    c.tw_modo = int64_t(1) << 62;
+    c.tw_a = tw_a;
+    c.tw_b = 0;
+    c.tw_c = tw_c;
+    c.tw_coff = coff;
+  };
   const int L = p->logn;
   const long long n = p->n;
   const float sc = inv ? (float)(1.0 / (double)n) : 1.f;
@@ -248,6 +264,7 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
     a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
     a.ncols = inner; a.O3 = outer; a.is_o3 = n * inner; a.is_j = inner;
     a.os_o3 = n * inner; a.os_k = inner; a.scale = sc;
+    if (tw) extra_tw(a, 1, 0);  // e = (coff + s) * k
     return launch_colpass(L, inv, 0, a, st);
   }
   // n = L1*L2, point n1 + L1*n2, output k2 + L2*k1 (out of place first pass)
@@ -264,6 +281,11 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
   b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
   b.ncols = inner; b.O1 = L2; b.O3 = outer; b.is_o1 = inner; b.is_o3 = n * inner; b.is_j = L2 * inner;
   b.os_o1 = inner; b.os_o3 = n * inner; b.os_k = L2 * inner; b.scale = sc;
+  // K = k2 + L2*k1 with k2 = o1 of this pass and k1 = its FFT index: e = (coff + s)*(o1 + L2*k)
+  if (tw) {
+    extra_tw(b, L2, 1);
+    b.tw_modo = L2;  // o1 ranges over k2 < L2
+  }
   return launch_colpass(l1, inv, 0, b, st);
 }
 
@@ -578,6 +600,28 @@ int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, con
   ga.C = yi; ga.bias = bi;
   e = launch_gemm_tf32(ga, st);
   if (e != cudaSuccess) return cuda_fail(e, "complex_linear: imaginary part");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re, const float* in_im,
+                            float* out_re, float* out_im, int64_t outer, int64_t inner, int inverse,
+                            int64_t col_offset, void* stream) {
+  if (!plan || !tw_plan) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: null plan");
+  if (outer < 0 || inner < 1 || col_offset < 0) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: bad sizes");
+  if (outer == 0) return TRNFFT_SUCCESS;
+  if (plan->logn < 1 || plan->logn > 2 * kMaxColLog)
+    return fail(TRNFFT_UNSUPPORTED, "exec_c2c_axis_tw: n=%lld (power of two up to 2^20 only)", (long long)plan->n);
+  if (!tw_plan->tw_hi) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: twiddle plan must be a power of two > 1024");
+  if (in_re == out_re || in_im == out_im)
+    return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: out of place only");
+  if (tw_plan->device != plan->device) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: plans on different devices");
+  int rc = check_ptrs("exec_c2c_axis_tw", {in_re, in_im, out_re, out_im}, 4);
+  if (rc) return rc;
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_c2c_axis_tw: cannot select device %d", plan->device);
+  cudaError_t e = run_axis(plan, in_re, in_im, out_re, out_im, outer, inner, inverse != 0,
+                           reinterpret_cast<cudaStream_t>(stream), tw_plan, col_offset);
+  if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_axis_tw");
   return TRNFFT_SUCCESS;
 }
 

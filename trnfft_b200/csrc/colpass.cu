@@ -122,8 +122,9 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
       float* __restrict__ qi = a.yi + base;
       const long long step = (long long)RSTEP * a.os_k;
       const float2* src = sm2 + cl * GM::PITCH;
-      const uint32_t de = B1 + C1 * (uint32_t)cg;
-      const uint32_t e0 = A1 * (uint32_t)cg + (uint32_t)r0 * de;
+      const uint32_t cgt = (uint32_t)(cg + a.tw_coff);
+      const uint32_t de = B1 + C1 * cgt;
+      const uint32_t e0 = A1 * cgt + (uint32_t)r0 * de;
       float2 w = make_float2(1.f, 0.f), d = w;
       if (tw) d = look((uint32_t)RSTEP * de);
 #pragma unroll
@@ -147,6 +148,7 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
       for (int q = 0; q < R; ++q) {
         const int k = q * THREADS + tid;
         const uint32_t mstep = A1 + C1 * (uint32_t)k;  // exponent step per column
+        const uint32_t coff = (uint32_t)a.tw_coff;
         float2 w = make_float2(1.f, 0.f), m = w;
         if (tw) m = look(mstep);
 #pragma unroll
@@ -155,8 +157,9 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
           if (cg < a.ncols) {
             float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
             if (tw) {
-              w = (c % kAnchor == 0) ? look(A1 * (uint32_t)cg + (uint32_t)k * (B1 + C1 * (uint32_t)cg))
-                                     : cmul(w, m);
+              w = (c % kAnchor == 0)
+                      ? look(A1 * ((uint32_t)cg + coff) + (uint32_t)k * (B1 + C1 * ((uint32_t)cg + coff)))
+                      : cmul(w, m);
               v = cmul(v, w);
             }
             const long long off = cg * a.os_c + k;
@@ -178,7 +181,8 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
         const long long cg = c0 + c;
         float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
         if (tw) {
-          w = (i % kAnchor == 0) ? look(A1 * (uint32_t)cg + (uint32_t)k * (B1 + C1 * (uint32_t)cg)) : cmul(w, m);
+          const uint32_t cgt = (uint32_t)cg + (uint32_t)a.tw_coff;
+          w = (i % kAnchor == 0) ? look(A1 * cgt + (uint32_t)k * (B1 + C1 * cgt)) : cmul(w, m);
           v = cmul(v, w);
         }
         if (cg < a.ncols) {

@@ -45,7 +45,8 @@ cudaError_t launch_bluestein(int logm, int mode, bool inv, const BlueArgs& a, cu
 //   kind 0: y + o1*os_o1 + o2*os_o2 + o3*os_o3 + c + k*os_k
 //   kind 1: y + o1*os_o1 + o2*os_o2 + o3*os_o3 + c*os_c + k
 // after multiplication by W_N^e,
-//   e = tw_mul*((o1 mod tw_modo)*(tw_a*c + tw_b*k) + tw_c*c*k)  (mod N),
+//   e = tw_mul*((o1 mod tw_modo)*(tw_a*c' + tw_b*k) + tw_c*c'*k)  (mod N),
+// c' = c + tw_coff,
 // with W_N^e = tw_hi[e >> tw_split] * tw_lo[e & (2^tw_split - 1)].
 struct ColArgs {
   const float* xr;
@@ -57,6 +58,7 @@ struct ColArgs {
   long long os_o1, os_o2, os_o3, os_k, os_c;
   int has_tw;
   long long tw_mul, tw_a, tw_b, tw_c, tw_modo;
+  long long tw_coff;  // added to the column index in the twiddle exponent
   long long nmask;
   int tw_split;
   const float2* tw_hi;

@@ -77,7 +77,7 @@ def _twiddle(yr, yi, n, col0, inverse):
     return yr * wr - yi * wi, yr * wi + yi * wr
 
 
-def _four_step(xr, xi, n, group, inverse, natural_order, col_fft, row_fft, columns_in=False):
+def _four_step(xr, xi, n, group, inverse, natural_order, col_fft, row_fft, columns_in=False, col_fft_tw=None):
     """Exchange skeleton of the distributed four-step FFT (see the module docstring).
 
     col_fft(re, im, inverse) transforms along dim 0 of [N1][C]; row_fft along dim 1 of [R][N2].
@@ -98,10 +98,12 @@ def _four_step(xr, xi, n, group, inverse, natural_order, col_fft, row_fft, colum
         si = xi.reshape(r1, P, c2).transpose(0, 1)
         ar = _a2a(sr, group).reshape(N1, c2)  # sources q in n1 order: [q][r1][c2] = [N1][c2]
         ai = _a2a(si, group).reshape(N1, c2)
-    # 2. transforms over n1 (down the columns)
-    yr, yi = col_fft(ar, ai, inverse)
-    # 3. twiddle W_N^{n2 k1}, n2 = p*c2 + c
-    yr, yi = _twiddle(yr, yi, n, p * c2, inverse)
+    # 2.+3. transforms over n1 (down the columns) and twiddle W_N^{n2 k1}, n2 = p*c2 + c
+    if col_fft_tw is not None:
+        yr, yi = col_fft_tw(ar, ai, inverse, n, p * c2)
+    else:
+        yr, yi = col_fft(ar, ai, inverse)
+        yr, yi = _twiddle(yr, yi, n, p * c2, inverse)
     # (for the inverse, 1/N comes from the two inverse transforms: 1/N1 and 1/N2)
     # 4. rows k1 of block q go to rank q: chunks are contiguous row blocks of [N1][c2]
     br = _a2a(yr, group).reshape(P, r1, c2).transpose(0, 1).reshape(r1, N2)
@@ -124,6 +126,22 @@ def _cuda_col_fft(re, im, inverse):
     from . import _ops
 
     return _ops.c2c_axis_raw(re.contiguous(), im.contiguous(), 0, inverse)
+
+
+def _cuda_col_fft_tw(re, im, inverse, n, col0):
+    """Column transforms with the four-step twiddle fused into their last pass."""
+    from . import _lib
+
+    re = re.contiguous()
+    im = im.contiguous()
+    n1, cols = re.shape
+    yr = torch.empty_like(re)
+    yi = torch.empty_like(im)
+    plan = _lib.device_plan(n1, re.device)
+    twp = _lib.device_plan(n, re.device)
+    _lib.call("trnfft_exec_c2c_axis_tw", plan.handle, twp.handle, _lib.ptr(re), _lib.ptr(im), _lib.ptr(yr),
+              _lib.ptr(yi), 1, cols, int(bool(inverse)), col0, _lib.stream_ptr(re.device))
+    return yr, yi
 
 
 def _cuda_row_fft(re, im, inverse):
@@ -153,7 +171,8 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
         raise ValueError("fft_distributed: n must be a power of two and every rank must hold n/P points")
     xr = x_local.real.reshape(-1).float().contiguous()
     xi = x_local.imag.reshape(-1).float().contiguous()
-    zr, zi = _four_step(xr, xi, n, group, inverse, natural_order, _cuda_col_fft, _cuda_row_fft, columns_in)
+    zr, zi = _four_step(xr, xi, n, group, inverse, natural_order, _cuda_col_fft, _cuda_row_fft, columns_in,
+                        col_fft_tw=_cuda_col_fft_tw)
     return ComplexTensor(zr, zi)
 
 
