@@ -5,7 +5,8 @@
 // by the window, runs a full complex FFT of each real frame, slices the
 // one-sided bins and transposes to (..., freq, time) -- five HBM round trips
 // of a tensor twice the signal's size.  Here one kernel reads each frame's
-// samples straight from the waveform (the padding is index arithmetic), applies
+// samples straight from the waveform (interior frames as aligned float2 pairs;
+// frames that reach into the padding map their indices by pad_mode), applies
 // the window, transforms the real frame as an n_fft/2-point complex FFT of
 // z[n] = x[2n] + i x[2n+1] plus an on-chip split, and writes the bins in the
 // (freq, time) layout: a block owns G consecutive frames of one waveform, so
@@ -19,9 +20,10 @@ template <int LOGM>
 struct StftGeom {
   static constexpr int LE = 4;
   using S = Sched<LOGM, LE>;
-  static constexpr int G0 = 256 / S::T;
+  static constexpr int G0 = 128 / S::T;
   static constexpr int G = G0 < 1 ? 1 : G0;  // frames per block
   static constexpr int THREADS = G * S::T;
+  static constexpr int MINB = THREADS >= 1024 ? 1 : 1024 / THREADS;
   static constexpr int FP = S::NP + 1;  // odd pitch: frame-strided smem reads avoid bank conflicts
   static constexpr size_t smem = (size_t)G * FP * sizeof(float2);
 };
@@ -46,7 +48,7 @@ __device__ __forceinline__ long long stft_src(long long i, long long L, int mode
 }
 
 template <int LOGM>
-__global__ void __launch_bounds__(StftGeom<LOGM>::THREADS) k_stft(StftArgs a) {
+__global__ void __launch_bounds__(StftGeom<LOGM>::THREADS, StftGeom<LOGM>::MINB) k_stft(StftArgs a) {
   using GM = StftGeom<LOGM>;
   using S = typename GM::S;
   constexpr int M = S::N;
@@ -66,15 +68,33 @@ __global__ void __launch_bounds__(StftGeom<LOGM>::THREADS) k_stft(StftArgs a) {
   const long long base = f * a.hop - a.pad;
 
   float vr[S::E], vi[S::E];
-  pass_load<LOGM, GM::LE, 0>(j, vr, vi, [&](int n, float& r, float& m) {
-    r = 0.f;
-    m = 0.f;
-    if (!valid) return;
-    const long long s0 = stft_src(base + 2 * n, a.len, a.pad_mode);
-    const long long s1 = stft_src(base + 2 * n + 1, a.len, a.pad_mode);
-    if (s0 >= 0) r = __ldg(x + s0) * __ldg(w + 2 * n);
-    if (s1 >= 0) m = __ldg(x + s1) * __ldg(w + 2 * n + 1);
-  });
+  // interior frames (no padding involved) with an even start read sample pairs as float2
+  const bool fast = valid && base >= 0 && base + N <= a.len && ((((uintptr_t)(x + base)) | (uintptr_t)w) & 7) == 0;
+  if (__syncthreads_and(fast || !valid)) {
+    const float2* x2 = reinterpret_cast<const float2*>(x + (valid ? base : 0));
+    const float2* w2 = reinterpret_cast<const float2*>(w);
+    pass_load<LOGM, GM::LE, 0>(j, vr, vi, [&](int n, float& r, float& m) {
+      if (valid) {
+        const float2 v = __ldg(x2 + n);
+        const float2 ww = __ldg(w2 + n);
+        r = v.x * ww.x;
+        m = v.y * ww.y;
+      } else {
+        r = 0.f;
+        m = 0.f;
+      }
+    });
+  } else {
+    pass_load<LOGM, GM::LE, 0>(j, vr, vi, [&](int n, float& r, float& m) {
+      r = 0.f;
+      m = 0.f;
+      if (!valid) return;
+      const long long s0 = stft_src(base + 2 * n, a.len, a.pad_mode);
+      const long long s1 = stft_src(base + 2 * n + 1, a.len, a.pad_mode);
+      if (s0 >= 0) r = __ldg(x + s0) * __ldg(w + 2 * n);
+      if (s1 >= 0) m = __ldg(x + s1) * __ldg(w + 2 * n + 1);
+    });
+  }
   pass_compute_store<LOGM, GM::LE, 0, false>(j, vr, vi, [&](int i, float r, float m) {
     sb[spad<S::SH>(i)] = make_float2(r, m);
   });
