@@ -93,10 +93,10 @@ __device__ __forceinline__ void fft_to_smem(int j, float2* sb, Ld ld) {
 
 // ----------------------------------------------------------------------------
 // Real -> complex, N = 2M.  Row t of x (length N) -> row t of y (H = M+1 bins).
-template <int LOGM, int LOGE>
-__global__ void __launch_bounds__(kRowThreads) k_r2c(RowArgs a) {
+template <int LOGM, int LOGE, int MINB = 1, int THR = kRowThreads>
+__global__ void __launch_bounds__(THR, MINB) k_r2c(RowArgs a) {
   using S = Sched<LOGM, LOGE>;
-  using GM = RowGeom<LOGM, LOGE>;
+  using GM = RowGeom<LOGM, LOGE, THR>;
   constexpr int M = S::N;
   constexpr int LOGN = LOGM + 1;
   extern __shared__ float sm[];
@@ -138,10 +138,10 @@ __global__ void __launch_bounds__(kRowThreads) k_r2c(RowArgs a) {
 
 // ----------------------------------------------------------------------------
 // Complex -> real, N = 2M.  Row t of the spectrum (bins 0..M) -> real row t.
-template <int LOGM, int LOGE>
-__global__ void __launch_bounds__(kRowThreads) k_c2r(RowArgs a) {
+template <int LOGM, int LOGE, int MINB = 1, int THR = kRowThreads>
+__global__ void __launch_bounds__(THR, MINB) k_c2r(RowArgs a) {
   using S = Sched<LOGM, LOGE>;
-  using GM = RowGeom<LOGM, LOGE>;
+  using GM = RowGeom<LOGM, LOGE, THR>;
   constexpr int M = S::N;
   constexpr int LOGN = LOGM + 1;
   extern __shared__ float sm[];
@@ -259,24 +259,29 @@ static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st, int variant) 
   return launch_c2c_v<LOGN, INV, RowVar<4, 1>>(a, st);
 }
 
-template <int LOGN>
-struct RowLogE {
-  static constexpr int v = 4;
-};
-
-template <int LOGM, int MODE>
-static cudaError_t launch_real_t(const RowArgs& a, cudaStream_t st) {
-  constexpr int LE = RowLogE<LOGM>::v;
-  using GM = RowGeom<LOGM, LE>;
-  auto kern = (MODE == 0) ? k_r2c<LOGM, LE> : k_c2r<LOGM, LE>;
+// Real transforms run an M = N/2 point complex FFT: same measured block shapes
+// as the complex kernel of that length.
+template <int LOGM, int MODE, class V>
+static cudaError_t launch_real_v(const RowArgs& a, cudaStream_t st) {
+  constexpr int LE = V::LOGE;
+  using GM = RowGeom<LOGM, LE, V::THR>;
+  auto kern = (MODE == 0) ? k_r2c<LOGM, LE, V::MINB, V::THR> : k_c2r<LOGM, LE, V::MINB, V::THR>;
   const size_t smem = GM::smem;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   const long long blocks = (a.batch + GM::G - 1) / GM::G;
-  kern<<<(unsigned)blocks, kRowThreads, smem, st>>>(a);
+  kern<<<(unsigned)blocks, V::THR, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int LOGM, int MODE>
+static cudaError_t launch_real_t(const RowArgs& a, cudaStream_t st) {
+  constexpr int v = default_row_variant<LOGM>();
+  if constexpr (v == 10) return launch_real_v<LOGM, MODE, RowVar<4, 6, 128>>(a, st);
+  if constexpr (v == 8) return launch_real_v<LOGM, MODE, RowVar<5, 4, 128>>(a, st);
+  return launch_real_v<LOGM, MODE, RowVar<4, 1>>(a, st);
 }
 
 cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st) {
