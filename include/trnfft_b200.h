@@ -164,13 +164,16 @@ TRNFFT_API int trnfft_complex_linear(const float* xr, const float* xi, const flo
 
 /* The column step of the four-step FFT across GPUs: transforms along the
  * middle axis of [outer][n][inner] (plan n, power of two <= 2^20, out of
- * place) and multiplies output (o, K, s) by W_M^{(col_offset + s) * K},
+ * place; ld_in / ld_out floats between the points of a column, 0 = inner,
+ * so a column sub-block of a wider array can be read and written densely)
+ * and multiplies output (o, K, s) by W_M^{(col_offset + s) * K},
  * M = tw_plan n (a power of two > 1024; its tables are used).  Replaces the
  * column DFTs + host twiddle of _stage_parallel_fft
  * (trnfft/nki/multicore.py:189-204) with one fused pass. */
 TRNFFT_API int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re,
                                        const float* in_im, float* out_re, float* out_im, int64_t outer,
-                                       int64_t inner, int inverse, int64_t col_offset, void* stream);
+                                       int64_t inner, int64_t ld_in, int64_t ld_out, int inverse,
+                                       int64_t col_offset, void* stream);
 
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex

@@ -150,7 +150,7 @@ def test_axis_with_fused_four_step_twiddle(n1, cols, col0, big, inverse):
     plan = _lib.device_plan(n1, xr.device)
     twp = _lib.device_plan(big, xr.device)
     _lib.call("trnfft_exec_c2c_axis_tw", plan.handle, twp.handle, _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(yr),
-              _lib.ptr(yi), 1, cols, int(inverse), col0, _lib.stream_ptr(xr.device))
+              _lib.ptr(yi), 1, cols, 0, 0, int(inverse), col0, _lib.stream_ptr(xr.device))
     xd = x.astype(np.complex128)
     f = np.fft.ifft(xd, axis=0) if inverse else np.fft.fft(xd, axis=0)
     k = np.arange(n1)[:, None]

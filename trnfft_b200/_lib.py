@@ -47,7 +47,7 @@ SIGNATURES = {
     "trnfft_exec_stft": (_INT, [_P, _P, _I64, _I64, _I64, _P, _INT, _INT, _INT, _INT, _I64, _P, _P, _P]),
     "trnfft_complex_linear_work_bytes": (_I64, [_I64, _I64, _I64]),
     "trnfft_complex_linear": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _INT, _P]),
-    "trnfft_exec_c2c_axis_tw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _INT, _I64, _P]),
+    "trnfft_exec_c2c_axis_tw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _I64, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
     "trnfft_exec_c2r": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
 }

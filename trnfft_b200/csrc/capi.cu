@@ -240,9 +240,13 @@ static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, c
 // Transforms along the middle axis of an [outer][n][inner] array, inner > 1.
 // tw (optional): after the transform, output (o, K, s) is multiplied by
 // W_{tw->n}^{(coff + s) * K} using tw's tables (the four-step inter-pass twiddle).
+// ld_in / ld_out: floats between consecutive points of one column (default inner).
 static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr, float* yi,
                             int64_t outer, int64_t inner, bool inv, cudaStream_t st,
-                            const trnfft_plan_s* tw = nullptr, int64_t coff = 0) {
+                            const trnfft_plan_s* tw = nullptr, int64_t coff = 0, int64_t ld_in = 0,
+                            int64_t ld_out = 0) {
+  if (ld_in <= 0) ld_in = inner;
+  if (ld_out <= 0) ld_out = inner;
   auto extra_tw = [&](ColArgs& c, long long tw_c, long long tw_a) {
     c.has_tw = 1;
     c.nmask = tw->n - 1;
@@ -262,8 +266,8 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
   if (L <= kMaxColLog) {
     ColArgs a = col_base(p);
     a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
-    a.ncols = inner; a.O3 = outer; a.is_o3 = n * inner; a.is_j = inner;
-    a.os_o3 = n * inner; a.os_k = inner; a.scale = sc;
+    a.ncols = inner; a.O3 = outer; a.is_o3 = n * ld_in; a.is_j = ld_in;
+    a.os_o3 = n * ld_out; a.os_k = ld_out; a.scale = sc;
     if (tw) extra_tw(a, 1, 0);  // e = (coff + s) * k
     return launch_colpass(L, inv, 0, a, st);
   }
@@ -272,15 +276,15 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
   const long long L1 = 1LL << l1, L2 = 1LL << l2;
   ColArgs a = col_base(p);  // FFT over n2; outer n1; output (n1*L2 + k2)*S + s; twiddle W_n^{n1 k2}
   a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
-  a.ncols = inner; a.O1 = L1; a.O3 = outer; a.is_o1 = inner; a.is_o3 = n * inner; a.is_j = L1 * inner;
-  a.os_o1 = L2 * inner; a.os_o3 = n * inner; a.os_k = inner;
+  a.ncols = inner; a.O1 = L1; a.O3 = outer; a.is_o1 = ld_in; a.is_o3 = n * ld_in; a.is_j = L1 * ld_in;
+  a.os_o1 = L2 * ld_out; a.os_o3 = n * ld_out; a.os_k = ld_out;
   a.has_tw = 1; a.tw_b = 1;
   cudaError_t e = launch_colpass(l2, inv, 0, a, st);
   if (e != cudaSuccess) return e;
   ColArgs b = col_base(p);  // FFT over n1 in place; outer k2
   b.xr = yr; b.xi = yi; b.yr = yr; b.yi = yi;
-  b.ncols = inner; b.O1 = L2; b.O3 = outer; b.is_o1 = inner; b.is_o3 = n * inner; b.is_j = L2 * inner;
-  b.os_o1 = inner; b.os_o3 = n * inner; b.os_k = L2 * inner; b.scale = sc;
+  b.ncols = inner; b.O1 = L2; b.O3 = outer; b.is_o1 = ld_out; b.is_o3 = n * ld_out; b.is_j = L2 * ld_out;
+  b.os_o1 = ld_out; b.os_o3 = n * ld_out; b.os_k = L2 * ld_out; b.scale = sc;
   // K = k2 + L2*k1 with k2 = o1 of this pass and k1 = its FFT index: e = (coff + s)*(o1 + L2*k)
   if (tw) {
     extra_tw(b, L2, 1);
@@ -604,10 +608,13 @@ int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, con
 }
 
 int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re, const float* in_im,
-                            float* out_re, float* out_im, int64_t outer, int64_t inner, int inverse,
-                            int64_t col_offset, void* stream) {
+                            float* out_re, float* out_im, int64_t outer, int64_t inner, int64_t ld_in,
+                            int64_t ld_out, int inverse, int64_t col_offset, void* stream) {
   if (!plan || !tw_plan) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: null plan");
   if (outer < 0 || inner < 1 || col_offset < 0) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: bad sizes");
+  if (ld_in == 0) ld_in = inner;
+  if (ld_out == 0) ld_out = inner;
+  if (ld_in < inner || ld_out < inner) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_axis_tw: ld < inner");
   if (outer == 0) return TRNFFT_SUCCESS;
   if (plan->logn < 1 || plan->logn > 2 * kMaxColLog)
     return fail(TRNFFT_UNSUPPORTED, "exec_c2c_axis_tw: n=%lld (power of two up to 2^20 only)", (long long)plan->n);
@@ -620,7 +627,7 @@ int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan, const flo
   DeviceGuard g(plan->device);
   if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_c2c_axis_tw: cannot select device %d", plan->device);
   cudaError_t e = run_axis(plan, in_re, in_im, out_re, out_im, outer, inner, inverse != 0,
-                           reinterpret_cast<cudaStream_t>(stream), tw_plan, col_offset);
+                           reinterpret_cast<cudaStream_t>(stream), tw_plan, col_offset, ld_in, ld_out);
   if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_axis_tw");
   return TRNFFT_SUCCESS;
 }

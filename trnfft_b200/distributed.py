@@ -26,6 +26,7 @@ exchange logic can be checked with CPU (gloo) ranks and a reference transform.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -144,6 +145,58 @@ def _cuda_col_fft_tw(re, im, inverse, n, col0):
     return yr, yi
 
 
+def _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks):
+    """CUDA four-step from the column block [N1][N2/P] with communication overlap.
+
+    The rank's columns are processed in `chunks` groups: the fused column FFT +
+    twiddle of group i+1 runs on the compute stream while group i's all-to-all
+    (async NCCL) is in flight; each received group is scattered into the row
+    layout [N1/P][N2] as soon as it lands.  Then the row transforms run.
+    """
+    from . import _lib, _ops
+
+    P, p = _world(group)
+    N1, N2 = _split_n(n)
+    r1, c2 = N1 // P, N2 // P
+    K = chunks if (chunks > 0 and c2 % chunks == 0) else 1
+    cw = c2 // K
+    dev = ar.device
+    plan = _lib.device_plan(N1, dev)
+    twp = _lib.device_plan(n, dev)
+    st = _lib.stream_ptr(dev)
+    rows_r = torch.empty(r1, N2, dtype=torch.float32, device=dev)
+    rows_i = torch.empty_like(rows_r)
+    vr = rows_r.view(r1, P, K, cw)
+    vi = rows_i.view(r1, P, K, cw)
+    pending = []
+    for ci in range(K):
+        yr = torch.empty(N1, cw, dtype=torch.float32, device=dev)
+        yi = torch.empty_like(yr)
+        off = ci * cw * 4
+        _lib.call("trnfft_exec_c2c_axis_tw", plan.handle, twp.handle, ctypes.c_void_p(ar.data_ptr() + off),
+                  ctypes.c_void_p(ai.data_ptr() + off), _lib.ptr(yr), _lib.ptr(yi), 1, cw, c2, cw,
+                  int(bool(inverse)), p * c2 + ci * cw, st)
+        rr = torch.empty(P, r1, cw, dtype=torch.float32, device=dev)
+        ri = torch.empty_like(rr)
+        w1 = dist.all_to_all_single(rr, yr, group=group, async_op=True)
+        w2 = dist.all_to_all_single(ri, yi, group=group, async_op=True)
+        pending.append((w1, w2, rr, ri, yr, yi))
+    for ci, (w1, w2, rr, ri, _yr, _yi) in enumerate(pending):
+        w1.wait()
+        w2.wait()
+        vr[:, :, ci, :].copy_(rr.permute(1, 0, 2))
+        vi[:, :, ci, :].copy_(ri.permute(1, 0, 2))
+    zr, zi = _ops.c2c_raw(rows_r, rows_i, inverse)
+    if not natural_order:
+        return zr, zi
+    tr = zr.reshape(r1, P, c2).transpose(0, 1)
+    ti = zi.reshape(r1, P, c2).transpose(0, 1)
+    gr = _a2a(tr, group).reshape(P, r1, c2)
+    gi = _a2a(ti, group).reshape(P, r1, c2)
+    return (gr.permute(2, 0, 1).reshape(c2 * N1).contiguous(),
+            gi.permute(2, 0, 1).reshape(c2 * N1).contiguous())
+
+
 def _cuda_row_fft(re, im, inverse):
     from . import _ops
 
@@ -159,7 +212,7 @@ def column_block(x_full_re: torch.Tensor, x_full_im: torch.Tensor, n: int, world
 
 
 def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natural_order: bool = True,
-                    group=None, columns_in: bool = False) -> ComplexTensor:
+                    group=None, columns_in: bool = False, chunks: int = 4) -> ComplexTensor:
     """Distributed 1-D FFT of length n = 2^k.
 
     Rank p passes its contiguous chunk of n/P points, or with ``columns_in`` its column block
@@ -171,8 +224,17 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
         raise ValueError("fft_distributed: n must be a power of two and every rank must hold n/P points")
     xr = x_local.real.reshape(-1).float().contiguous()
     xi = x_local.imag.reshape(-1).float().contiguous()
-    zr, zi = _four_step(xr, xi, n, group, inverse, natural_order, _cuda_col_fft, _cuda_row_fft, columns_in,
-                        col_fft_tw=_cuda_col_fft_tw)
+    N1, N2 = _split_n(n)
+    if N1 % P or N2 % P:
+        raise ValueError(f"N={n} (= {N1} x {N2}) must split evenly over {P} ranks")
+    c2 = N2 // P
+    if columns_in:
+        ar, ai = xr.reshape(N1, c2), xi.reshape(N1, c2)
+    else:
+        r1 = N1 // P
+        ar = _a2a(xr.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
+        ai = _a2a(xi.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
+    zr, zi = _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks)
     return ComplexTensor(zr, zi)
 
 
