@@ -83,6 +83,14 @@ def test_real_roundtrip_and_fp64(n):
     assert rel_l2(host(y), O.irfft(sr, si, n=n, precision="double")) < TOL
 
 
-def test_too_long_raises_cleanly():
-    with pytest.raises(NotImplementedError):
-        trnfft.fft(torch.randn(2, 8193, device="cuda"))
+@pytest.mark.parametrize("n,batch", [(8193, 3), (10007, 2), (100003, 1), (1 << 20 | 1, 1)])
+def test_multipass_bluestein_vs_fp64(n, batch):
+    """Lengths beyond the fused kernel (padded m > 16384): multi-pass Bluestein."""
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal((batch, n)) + 1j * rng.standard_normal((batch, n))).astype(np.complex64)
+    X = trnfft.fft(ComplexTensor(cuda(x.real), cuda(x.imag)))
+    assert rel_l2(cplx(X), np.fft.fft(x.astype(np.complex128))) < 5e-6
+    Z = trnfft.ifft(ComplexTensor(cuda(x.real), cuda(x.imag)))
+    assert rel_l2(cplx(Z), np.fft.ifft(x.astype(np.complex128))) < 5e-6
+    r = trnfft.rfft(cuda(x.real))
+    assert rel_l2(cplx(r), np.fft.rfft(x.real.astype(np.float64))) < 5e-6

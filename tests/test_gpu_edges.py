@@ -78,7 +78,14 @@ def test_irfft_longer_spectrum_uses_hermitian_part():
 
 
 def test_unsupported_sizes_raise_cleanly():
+    """Lengths past the supported range fail with a clear error before any launch."""
+    from trnfft_b200 import _lib
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    plan = _lib.DevicePlan((1 << 31) + 1, dev.index)  # Bluestein padding would be 2^33
+    t = torch.zeros(4, device=dev)
     with pytest.raises(NotImplementedError):
-        trnfft.fft(torch.randn(1, 9001, device="cuda"))
+        _lib.call("trnfft_exec_c2c", plan.handle, _lib.ptr(t), _lib.ptr(t), _lib.ptr(t), _lib.ptr(t), 1, 0,
+                  None, _lib.stream_ptr(dev))
     with pytest.raises(ValueError):
         trnfft.set_small_n_algorithm("nope")

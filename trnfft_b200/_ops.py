@@ -79,9 +79,12 @@ def c2c_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool) -> tuple[torch.Te
     batch = a.shape[0]
     if batch and n:
         plan = _lib.device_plan(n, a.device)
-        # out of place: no work area is needed
+        # out-of-place calls need a work area only for multi-pass Bluestein (m > 16384)
+        work = None
+        if plan.algorithm == _lib.ALG_BLUESTEIN and plan.padded_n > 16384:
+            work = torch.empty(plan.work_bytes(batch), dtype=torch.uint8, device=a.device)
         _lib.call("trnfft_exec_c2c", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi),
-                  batch, int(bool(inverse)), None, _lib.stream_ptr(a.device))
+                  batch, int(bool(inverse)), _lib.ptr(work), _lib.stream_ptr(a.device))
     return yr.reshape(shape), yi.reshape(shape)
 
 

@@ -237,6 +237,13 @@ static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, c
   return cudaSuccess;
 }
 
+static int run_rows_multipass_plan(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr, float* yi,
+                                   int64_t batch, bool inv, cudaStream_t st) {
+  cudaError_t e = run_rows_multipass(p, xr, xi, yr, yi, batch, inv, st);
+  if (e != cudaSuccess) return cuda_fail(e, "multi-pass transform");
+  return TRNFFT_SUCCESS;
+}
+
 // Transforms along the middle axis of an [outer][n][inner] array, inner > 1.
 // tw (optional): after the transform, output (o, K, s) is multiplied by
 // W_{tw->n}^{(coff + s) * K} using tw's tables (the four-step inter-pass twiddle).
@@ -323,6 +330,52 @@ static int make_bluestein_tables(trnfft_plan_s* p) {
 
 static constexpr int kMaxBluesteinLogM = 14;
 
+static int run_rows_multipass_plan(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr, float* yi,
+                                   int64_t batch, bool inv, cudaStream_t st);
+
+// Bluestein with m > 16384: chirp (n, float2), an m-point sub-plan, and
+// H = FFT_m(h) computed on the device by the multi-pass kernels (planar).
+static int make_large_bluestein(trnfft_plan_s* p) {
+  const int64_t n = p->n, m = p->m;
+  std::vector<float2> c(n);
+  std::vector<float> hr(m, 0.f), hi(m, 0.f);
+  for (int64_t k = 0; k < n; ++k) {
+    const int64_t e = (k * k) % (2 * n);
+    const double ang = -M_PI * (double)e / (double)n;
+    c[k] = make_float2((float)std::cos(ang), (float)std::sin(ang));
+  }
+  for (int64_t j = 0; j < n; ++j) {
+    hr[j] = c[j].x;
+    hi[j] = -c[j].y;
+  }
+  for (int64_t j = 1; j < n; ++j) {
+    hr[m - j] = c[j].x;
+    hi[m - j] = -c[j].y;
+  }
+  trnfft_plan_t sub = nullptr;
+  int rc = trnfft_plan_create(&sub, m, p->device);
+  if (rc) return rc;
+  p->sub = sub;
+  float *dh = nullptr;
+  cudaError_t e = cudaMalloc(&p->chirp, sizeof(float2) * n);
+  if (e == cudaSuccess) e = cudaMalloc(&p->Hr, sizeof(float) * m);
+  if (e == cudaSuccess) e = cudaMalloc(&p->Hi, sizeof(float) * m);
+  if (e == cudaSuccess) e = cudaMalloc(&dh, sizeof(float) * 2 * m);
+  if (e != cudaSuccess) {
+    if (dh) cudaFree(dh);
+    return fail(TRNFFT_ALLOC_FAILED, "plan_create: %s", cudaGetErrorString(e));
+  }
+  e = cudaMemcpy(p->chirp, c.data(), sizeof(float2) * n, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dh, hr.data(), sizeof(float) * m, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(dh + m, hi.data(), sizeof(float) * m, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) rc = run_rows_multipass_plan(sub, dh, dh + m, p->Hr, p->Hi, 1, false, 0);
+  if (e == cudaSuccess && rc == TRNFFT_SUCCESS) e = cudaDeviceSynchronize();
+  cudaFree(dh);
+  if (rc) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "plan_create: Bluestein filter spectrum");
+  return TRNFFT_SUCCESS;
+}
+
 extern "C" {
 
 int trnfft_abi_version(void) { return TRNFFT_B200_ABI_VERSION; }
@@ -365,6 +418,12 @@ int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device) {
         trnfft_plan_destroy(p);
         return rc2;
       }
+    } else if (bl <= kMaxMultipassLog) {
+      int rc2 = make_large_bluestein(p);
+      if (rc2) {
+        trnfft_plan_destroy(p);
+        return rc2;
+      }
     }
   }
   if (p->logn > kMaxColLog && p->logn <= kMaxMultipassLog) {
@@ -400,11 +459,14 @@ int trnfft_plan_destroy(trnfft_plan_t plan) {
     if (plan->chirp) cudaFree(plan->chirp);
     if (plan->H) cudaFree(plan->H);
   }
-  if (plan->tw_hi || plan->tw_lo) {
+  if (plan->tw_hi || plan->tw_lo || plan->Hr || plan->Hi) {
     DeviceGuard g(plan->device);
     if (plan->tw_hi) cudaFree(plan->tw_hi);
     if (plan->tw_lo) cudaFree(plan->tw_lo);
+    if (plan->Hr) cudaFree(plan->Hr);
+    if (plan->Hi) cudaFree(plan->Hi);
   }
+  if (plan->sub) trnfft_plan_destroy(plan->sub);
   delete plan;
   return TRNFFT_SUCCESS;
 }
@@ -414,9 +476,16 @@ int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* padded_n, int
   if (!plan) return fail(TRNFFT_INVALID_VALUE, "plan_query: null plan");
   if (algorithm) *algorithm = plan->algorithm;
   if (padded_n) *padded_n = plan->algorithm == TRNFFT_ALG_BLUESTEIN ? plan->m : plan->n;
-  // Only an in-place multi-pass transform needs a work area (a copy of the input).
-  if (work_bytes)
-    *work_bytes = plan->algorithm == TRNFFT_ALG_MULTIPASS ? (int64_t)(2 * sizeof(float)) * plan->n * batch : 0;
+  // An in-place multi-pass transform needs a work area (a copy of the input);
+  // a multi-pass Bluestein transform (m > 16384) always needs two m-point buffers.
+  if (work_bytes) {
+    if (plan->algorithm == TRNFFT_ALG_MULTIPASS)
+      *work_bytes = (int64_t)(2 * sizeof(float)) * plan->n * batch;
+    else if (plan->algorithm == TRNFFT_ALG_BLUESTEIN && plan->sub)
+      *work_bytes = (int64_t)(4 * sizeof(float)) * plan->m * batch;
+    else
+      *work_bytes = 0;
+  }
   return TRNFFT_SUCCESS;
 }
 
@@ -484,9 +553,26 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
       break;
     }
     case TRNFFT_ALG_BLUESTEIN: {
+      if (plan->sub) {
+        if (!work) return fail(TRNFFT_INVALID_VALUE, "exec_c2c: Bluestein n=%lld needs the work area", (long long)n);
+        const size_t mb = (size_t)plan->m * (size_t)batch;
+        float* ar = static_cast<float*>(work);
+        float *ai = ar + mb, *br = ai + mb, *bi = br + mb;
+        const bool inv = inverse != 0;
+        e = launch_blue_pre(in_re, in_im, plan->chirp, ar, ai, batch, n, plan->m, inv, st);
+        if (e == cudaSuccess && run_rows_multipass_plan(plan->sub, ar, ai, br, bi, batch, false, st))
+          return TRNFFT_CUDA_ERROR;
+        if (e == cudaSuccess) e = launch_blue_mul(br, bi, plan->Hr, plan->Hi, batch, plan->m, inv, st);
+        if (e == cudaSuccess && run_rows_multipass_plan(plan->sub, br, bi, ar, ai, batch, true, st))
+          return TRNFFT_CUDA_ERROR;
+        if (e == cudaSuccess)
+          e = launch_blue_post(ar, ai, plan->chirp, out_re, out_im, batch, n, plan->m, inv,
+                               inv ? (float)(1.0 / (double)n) : 1.f, st);
+        break;
+      }
       if (!plan->H)
-        return fail(TRNFFT_UNSUPPORTED, "exec_c2c: Bluestein length n=%lld (padded %lld) above the fused "
-                    "kernel's limit n <= 8192", (long long)n, (long long)plan->m);
+        return fail(TRNFFT_UNSUPPORTED, "exec_c2c: Bluestein length n=%lld (padded %lld) above the supported "
+                    "2^%d", (long long)n, (long long)plan->m, kMaxMultipassLog);
       BlueArgs a{in_re, in_im, out_re, out_im, batch, (int)n, plan->chirp, plan->H};
       e = launch_bluestein(plan->logm, 0, inverse != 0, a, st);
       break;

@@ -105,6 +105,14 @@ struct GemmArgs {
 cudaError_t launch_gemm_tf32(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_split_tf32(const float* x, float* hi, float* lo, long long n, float scale, cudaStream_t st);
 
+// Multi-pass Bluestein helpers (bluestein_large.cu).
+cudaError_t launch_blue_pre(const float* xr, const float* xi, const float2* chirp, float* ar, float* ai,
+                            long long batch, long long n, long long m, bool inv, cudaStream_t st);
+cudaError_t launch_blue_mul(float* br, float* bi, const float* hr, const float* hi, long long batch, long long m,
+                            bool inv, cudaStream_t st);
+cudaError_t launch_blue_post(const float* ar, const float* ai, const float2* chirp, float* yr, float* yi,
+                             long long batch, long long n, long long m, bool inv, float scale, cudaStream_t st);
+
 cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t st);
 bool rows_c2c_tma_ok(int logn, const RowArgs& a);
 cudaError_t launch_rows_c2c_tma(int logn, bool inv, const RowArgs& a, cudaStream_t st);

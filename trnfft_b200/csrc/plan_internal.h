@@ -18,4 +18,8 @@ struct trnfft_plan_s {
   float2* tw_hi = nullptr;  // power of two n > 1024: W_n^(i << tw_split)
   float2* tw_lo = nullptr;  // power of two n > 1024: W_n^i, i < 2^tw_split
   int tw_split = 0;
+  // Bluestein with m > 16384 (multi-pass): m-point sub-plan and H = FFT_m(h), planar
+  struct trnfft_plan_s* sub = nullptr;
+  float* Hr = nullptr;
+  float* Hi = nullptr;
 };
