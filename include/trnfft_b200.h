@@ -175,6 +175,34 @@ TRNFFT_API int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan
                                        int64_t inner, int64_t ld_in, int64_t ld_out, int inverse,
                                        int64_t col_offset, void* stream);
 
+/* Exchange buffers for the four-step FFT across GPUs, shared between
+ * processes with CUDA IPC (no multicast objects).  trnfft_xbuf_alloc
+ * allocates `bytes` on `device` and writes its IPC handle
+ * (trnfft_ipc_handle_bytes() bytes) to ipc_handle; trnfft_ipc_open maps a
+ * peer's buffer on `device`.  No counterpart in the reference (its
+ * multi-core path has no collectives, trnfft/nki/multicore.py:39-55). */
+TRNFFT_API int trnfft_ipc_handle_bytes(void);
+TRNFFT_API int trnfft_xbuf_alloc(int device, int64_t bytes, void** ptr, void* ipc_handle);
+TRNFFT_API int trnfft_xbuf_free(int device, void* ptr);
+TRNFFT_API int trnfft_ipc_open(int device, const void* ipc_handle, void** ptr);
+TRNFFT_API int trnfft_ipc_close(int device, void* ptr);
+
+/* The column step of the four-step FFT across `npeers` GPUs with the
+ * exchange fused in: like trnfft_exec_c2c_axis_tw on this rank's column
+ * block [n][inner] (ld_in floats per point), but the output of global row
+ * K (0 <= K < n) is stored by this kernel into rank K / rows_per_peer's row
+ * buffer peer_re/peer_im[q] at row K % rows_per_peer, columns
+ * peer_col0 .. peer_col0+inner (peer_ld floats per row): NVLink peer stores
+ * replace the all-to-all of the reference's host-side transpose
+ * (trnfft/nki/multicore.py:189-217).  The caller orders the ranks before
+ * (peers done reading) and after (all stores landed) the call.  n > 1024
+ * needs `work` of 2*n*inner floats. */
+TRNFFT_API int trnfft_exec_fourstep_scatter(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re,
+                                            const float* in_im, int64_t inner, int64_t ld_in, int inverse,
+                                            int64_t col_offset, int npeers, float* const* peer_re,
+                                            float* const* peer_im, int64_t rows_per_peer, int64_t peer_ld,
+                                            int64_t peer_col0, void* work, void* stream);
+
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex
  * transform of the real row and keeps the first n//2+1 bins. */

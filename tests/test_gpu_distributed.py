@@ -43,6 +43,10 @@ def _worker(rank, world, port, q):
     cr, ci = D.column_block(xr, xi, n, world, rank)
     y = D.fft_distributed(ComplexTensor(cr, ci), n, columns_in=True)
     res["cols"] = (y.real.cpu().numpy(), y.imag.cpu().numpy())
+    y = D.fft_distributed(ComplexTensor(cr, ci), n, columns_in=True, exchange="nccl")
+    res["cols_nccl"] = (y.real.cpu().numpy(), y.imag.cpu().numpy())
+    y = D.fft_distributed(ComplexTensor(xr[lo:hi], xi[lo:hi]), n)  # second call reuses the mapped buffers
+    res["nat2"] = (y.real.cpu().numpy(), y.imag.cpu().numpy())
     z = D.fft_distributed(ComplexTensor(xr[lo:hi], xi[lo:hi]), n, inverse=True)
     res["inv"] = (z.real.cpu().numpy(), z.imag.cpu().numpy())
     H, W = 2048, 4096
@@ -86,6 +90,8 @@ def test_two_gpu_four_step_and_fft2():
 
     assert rel(cat("nat"), ref) < 2e-6
     assert rel(cat("cols"), ref) < 2e-6
+    assert rel(cat("cols_nccl"), ref) < 2e-6
+    assert rel(cat("nat2"), ref) < 2e-6
     assert rel(cat("inv"), np.fft.ifft(x)) < 2e-6
     H, W = 2048, 4096
     f = (rng.standard_normal((H, W)) + 1j * rng.standard_normal((H, W))).astype(np.complex64).astype(np.complex128)

@@ -48,6 +48,13 @@ SIGNATURES = {
     "trnfft_complex_linear_work_bytes": (_I64, [_I64, _I64, _I64]),
     "trnfft_complex_linear": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _INT, _P]),
     "trnfft_exec_c2c_axis_tw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _I64, _P]),
+    "trnfft_ipc_handle_bytes": (_INT, []),
+    "trnfft_xbuf_alloc": (_INT, [_INT, _I64, ctypes.POINTER(_P), _P]),
+    "trnfft_xbuf_free": (_INT, [_INT, _P]),
+    "trnfft_ipc_open": (_INT, [_INT, _P, ctypes.POINTER(_P)]),
+    "trnfft_ipc_close": (_INT, [_INT, _P]),
+    "trnfft_exec_fourstep_scatter": (_INT, [_P, _P, _P, _P, _I64, _I64, _INT, _I64, _INT,
+                                            ctypes.POINTER(_P), ctypes.POINTER(_P), _I64, _I64, _I64, _P, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
     "trnfft_exec_c2r": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
 }

@@ -247,11 +247,33 @@ static int run_rows_multipass_plan(const trnfft_plan_s* p, const float* xr, cons
 // Transforms along the middle axis of an [outer][n][inner] array, inner > 1.
 // tw (optional): after the transform, output (o, K, s) is multiplied by
 // W_{tw->n}^{(coff + s) * K} using tw's tables (the four-step inter-pass twiddle).
+// Peer scatter of the last pass (four-step exchange over NVLink), see ColArgs kind 2.
+struct ScatterSpec {
+  int npeers;
+  float* re[8];
+  float* im[8];
+  long long rows, ld, col0;
+};
+
 // ld_in / ld_out: floats between consecutive points of one column (default inner).
+// With sc, the last pass stores into the peers' row buffers instead of yr/yi
+// (yr/yi then only hold the first pass's output when there are two passes).
 static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr, float* yi,
                             int64_t outer, int64_t inner, bool inv, cudaStream_t st,
                             const trnfft_plan_s* tw = nullptr, int64_t coff = 0, int64_t ld_in = 0,
-                            int64_t ld_out = 0) {
+                            int64_t ld_out = 0, const ScatterSpec* scs = nullptr) {
+  auto scatter = [&](ColArgs& c, long long ka, long long kb) {
+    c.sc_npeers = scs->npeers;
+    for (int q = 0; q < scs->npeers; ++q) {
+      c.sc_re[q] = scs->re[q];
+      c.sc_im[q] = scs->im[q];
+    }
+    c.sc_ka = ka;
+    c.sc_kb = kb;
+    c.sc_rows = scs->rows;
+    c.sc_ld = scs->ld;
+    c.sc_col0 = scs->col0;
+  };
   if (ld_in <= 0) ld_in = inner;
   if (ld_out <= 0) ld_out = inner;
   auto extra_tw = [&](ColArgs& c, long long tw_c, long long tw_a) {
@@ -276,6 +298,10 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
     a.ncols = inner; a.O3 = outer; a.is_o3 = n * ld_in; a.is_j = ld_in;
     a.os_o3 = n * ld_out; a.os_k = ld_out; a.scale = sc;
     if (tw) extra_tw(a, 1, 0);  // e = (coff + s) * k
+    if (scs) {
+      scatter(a, 0, 1);  // K = k
+      return launch_colpass(L, inv, 2, a, st);
+    }
     return launch_colpass(L, inv, 0, a, st);
   }
   // n = L1*L2, point n1 + L1*n2, output k2 + L2*k1 (out of place first pass)
@@ -296,6 +322,10 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
   if (tw) {
     extra_tw(b, L2, 1);
     b.tw_modo = L2;  // o1 ranges over k2 < L2
+  }
+  if (scs) {
+    scatter(b, 1, L2);  // K = k2 + L2*k1 with k2 = o1
+    return launch_colpass(l1, inv, 2, b, st);
   }
   return launch_colpass(l1, inv, 0, b, st);
 }
@@ -715,6 +745,86 @@ int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan, const flo
   cudaError_t e = run_axis(plan, in_re, in_im, out_re, out_im, outer, inner, inverse != 0,
                            reinterpret_cast<cudaStream_t>(stream), tw_plan, col_offset, ld_in, ld_out);
   if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_axis_tw");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_xbuf_alloc(int device, int64_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes <= 0) return fail(TRNFFT_INVALID_VALUE, "xbuf_alloc: bad arguments");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "xbuf_alloc: cannot select device %d", device);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return fail(TRNFFT_ALLOC_FAILED, "xbuf_alloc: %s", cudaGetErrorString(e));
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "xbuf_alloc: cudaIpcGetMemHandle");
+  }
+  std::memcpy(ipc_handle, &h, sizeof h);
+  *ptr = p;
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_xbuf_free(int device, void* ptr) {
+  DeviceGuard g(device);
+  if (ptr) cudaFree(ptr);
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_ipc_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int trnfft_ipc_open(int device, const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return fail(TRNFFT_INVALID_VALUE, "ipc_open: null argument");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "ipc_open: cannot select device %d", device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof h);
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "ipc_open: cudaIpcOpenMemHandle");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_ipc_close(int device, void* ptr) {
+  DeviceGuard g(device);
+  if (ptr) cudaIpcCloseMemHandle(ptr);
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_exec_fourstep_scatter(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re, const float* in_im,
+                                 int64_t inner, int64_t ld_in, int inverse, int64_t col_offset, int npeers,
+                                 float* const* peer_re, float* const* peer_im, int64_t rows_per_peer,
+                                 int64_t peer_ld, int64_t peer_col0, void* work, void* stream) {
+  if (!plan || !tw_plan || !peer_re || !peer_im) return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: null argument");
+  if (npeers < 1 || npeers > 8) return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: 1..8 peers");
+  if (plan->logn < 1 || plan->logn > 2 * kMaxColLog || !tw_plan->tw_hi)
+    return fail(TRNFFT_UNSUPPORTED, "fourstep_scatter: column length must be a power of two <= 2^20");
+  if (inner < 1 || ld_in < inner || rows_per_peer * npeers != plan->n || peer_ld < peer_col0 + inner)
+    return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: inconsistent sizes");
+  int rc = check_ptrs("fourstep_scatter", {in_re, in_im}, 4);
+  if (rc) return rc;
+  ScatterSpec sc;
+  sc.npeers = npeers;
+  for (int q = 0; q < npeers; ++q) {
+    if (!peer_re[q] || !peer_im[q]) return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: null peer buffer");
+    sc.re[q] = peer_re[q];
+    sc.im[q] = peer_im[q];
+  }
+  sc.rows = rows_per_peer;
+  sc.ld = peer_ld;
+  sc.col0 = peer_col0;
+  float* tr = nullptr;
+  float* ti = nullptr;
+  if (plan->logn > kMaxColLog) {
+    if (!work) return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: n > 1024 needs the work area");
+    tr = static_cast<float*>(work);
+    ti = tr + (size_t)plan->n * inner;
+  }
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "fourstep_scatter: cannot select device %d", plan->device);
+  cudaError_t e = run_axis(plan, in_re, in_im, tr, ti, 1, inner, inverse != 0, reinterpret_cast<cudaStream_t>(stream),
+                           tw_plan, col_offset, ld_in, inner, &sc);
+  if (e != cudaSuccess) return cuda_fail(e, "fourstep_scatter");
   return TRNFFT_SUCCESS;
 }
 

@@ -113,7 +113,36 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
     if (INV) w.y = -w.y;
     return w;
   };
-  if constexpr (KIND == 0) {
+  if constexpr (KIND == 2) {
+    // column-wise like kind 0, each output stored into its owner rank's row
+    // buffer (peer memory over NVLink for the other ranks)
+    if (colok) {
+      const long long cg = c0 + cl;
+      const float2* src = sm2 + cl * GM::PITCH;
+      const uint32_t cgt = (uint32_t)(cg + a.tw_coff);
+      const uint32_t de = B1 + C1 * cgt;
+      const uint32_t e0 = A1 * cgt + (uint32_t)r0 * de;
+      float2 w = make_float2(1.f, 0.f), d = w;
+      if (tw) d = look((uint32_t)RSTEP * de);
+#pragma unroll
+      for (int i = 0; i < ITER; ++i) {
+        const int k = r0 + i * RSTEP;
+        float2 v = src[spad<S::SH>(k)];
+        if (tw) {
+          w = (i % kAnchor == 0) ? look(e0 + (uint32_t)i * RSTEP * de) : cmul(w, d);
+          v = cmul(v, w);
+        }
+        const long long K = o1 * a.sc_ka + (long long)k * a.sc_kb;
+        const int q = (int)(K / a.sc_rows);
+        const long long off = (K - (long long)q * a.sc_rows) * a.sc_ld + a.sc_col0 + cg;
+        if (q < a.sc_npeers) {
+          a.sc_re[q][off] = v.x * sc;
+          a.sc_im[q][off] = v.y * sc;
+        }
+      }
+    }
+    __threadfence_system();
+  } else if constexpr (KIND == 0) {
     // column-wise, same thread mapping as the load: k = r0 + i*RSTEP
     if (colok) {
       const long long cg = c0 + cl;
@@ -216,6 +245,7 @@ static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
 template <int LOGL>
 static cudaError_t launch_col_l(bool inv, int kind, const ColArgs& a, cudaStream_t st) {
   if (kind == 0) return inv ? launch_col_t<LOGL, true, 0>(a, st) : launch_col_t<LOGL, false, 0>(a, st);
+  if (kind == 2) return inv ? launch_col_t<LOGL, true, 2>(a, st) : launch_col_t<LOGL, false, 2>(a, st);
   return inv ? launch_col_t<LOGL, true, 1>(a, st) : launch_col_t<LOGL, false, 1>(a, st);
 }
 

@@ -197,6 +197,101 @@ def _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks):
             gi.permute(2, 0, 1).reshape(c2 * N1).contiguous())
 
 
+class _PeerExchange:
+    """Row buffers [N1/P][N2] on every rank, mapped into every other rank by CUDA IPC."""
+
+    def __init__(self, n, group, dev):
+        from . import _lib
+
+        P, p = _world(group)
+        N1, N2 = _split_n(n)
+        self.rows, self.cols = N1 // P, N2
+        nbytes = self.rows * self.cols * 4
+        lib = _lib.load()
+        hb = lib.trnfft_ipc_handle_bytes()
+        self.dev = dev
+        self.local = []
+        handles = []
+        for _ in range(2):
+            ptr = ctypes.c_void_p()
+            h = ctypes.create_string_buffer(hb)
+            _lib.call("trnfft_xbuf_alloc", dev.index, nbytes, ctypes.byref(ptr), h)
+            self.local.append(ptr)
+            handles.append(h.raw)
+        everyone = [None] * P
+        dist.all_gather_object(everyone, handles, group=group)
+        self.opened = []
+        self.peer_re = (ctypes.c_void_p * P)()
+        self.peer_im = (ctypes.c_void_p * P)()
+        for q in range(P):
+            if q == p:
+                self.peer_re[q], self.peer_im[q] = self.local[0].value, self.local[1].value
+                continue
+            ptrs = []
+            for plane in range(2):
+                ptr = ctypes.c_void_p()
+                _lib.call("trnfft_ipc_open", dev.index, ctypes.create_string_buffer(everyone[q][plane], hb),
+                          ctypes.byref(ptr))
+                self.opened.append(ptr)
+                ptrs.append(ptr.value)
+            self.peer_re[q], self.peer_im[q] = ptrs
+
+    def __del__(self):
+        try:
+            from . import _lib
+
+            for ptr in self.opened:
+                _lib.load().trnfft_ipc_close(self.dev.index, ptr)
+            for ptr in self.local:
+                _lib.load().trnfft_xbuf_free(self.dev.index, ptr)
+        except Exception:
+            pass
+
+
+_exchanges: dict = {}
+
+
+def _device_barrier(group, dev):
+    """Stream-ordered cross-rank barrier: a one-element NCCL all-reduce."""
+    t = torch.zeros(1, device=dev)
+    dist.all_reduce(t, group=group)
+
+
+def _four_step_peer(ar, ai, n, group, inverse, natural_order):
+    """CUDA four-step with the exchange inside the column kernel (NVLink peer stores)."""
+    from . import _lib
+
+    P, p = _world(group)
+    N1, N2 = _split_n(n)
+    r1, c2 = N1 // P, N2 // P
+    dev = ar.device
+    key = (n, P, dev.index, id(group))
+    ex = _exchanges.get(key)
+    if ex is None:
+        ex = _exchanges[key] = _PeerExchange(n, group, dev)
+    plan = _lib.device_plan(N1, dev)
+    twp = _lib.device_plan(n, dev)
+    work = torch.empty(2 * N1 * c2, dtype=torch.float32, device=dev) if N1 > 1024 else None
+    _device_barrier(group, dev)  # every rank has finished reading its row buffer
+    _lib.call("trnfft_exec_fourstep_scatter", plan.handle, twp.handle, _lib.ptr(ar), _lib.ptr(ai), c2, c2,
+              int(bool(inverse)), p * c2, P, ex.peer_re, ex.peer_im, r1, N2, p * c2, _lib.ptr(work),
+              _lib.stream_ptr(dev))
+    _device_barrier(group, dev)  # every rank's stores have landed
+    zr = torch.empty(r1, N2, dtype=torch.float32, device=dev)
+    zi = torch.empty_like(zr)
+    rplan = _lib.device_plan(N2, dev)
+    _lib.call("trnfft_exec_c2c", rplan.handle, ex.local[0], ex.local[1], _lib.ptr(zr), _lib.ptr(zi), r1,
+              int(bool(inverse)), None, _lib.stream_ptr(dev))
+    if not natural_order:
+        return zr, zi
+    tr = zr.reshape(r1, P, c2).transpose(0, 1)
+    ti = zi.reshape(r1, P, c2).transpose(0, 1)
+    gr = _a2a(tr, group).reshape(P, r1, c2)
+    gi = _a2a(ti, group).reshape(P, r1, c2)
+    return (gr.permute(2, 0, 1).reshape(c2 * N1).contiguous(),
+            gi.permute(2, 0, 1).reshape(c2 * N1).contiguous())
+
+
 def _cuda_row_fft(re, im, inverse):
     from . import _ops
 
@@ -212,12 +307,16 @@ def column_block(x_full_re: torch.Tensor, x_full_im: torch.Tensor, n: int, world
 
 
 def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natural_order: bool = True,
-                    group=None, columns_in: bool = False, chunks: int = 4) -> ComplexTensor:
+                    group=None, columns_in: bool = False, chunks: int = 4, exchange: str = "peer") -> ComplexTensor:
     """Distributed 1-D FFT of length n = 2^k.
 
     Rank p passes its contiguous chunk of n/P points, or with ``columns_in`` its column block
     [N1][N2/P] (``column_block``), which saves one all-to-all.  The result is the contiguous
     chunk of X (``natural_order``) or X[k1 + N1*k2] for k1 in block p stored [k1][k2].
+
+    ``exchange="peer"`` (default, one node): the column kernel stores its output straight into
+    the owning ranks' row buffers over NVLink (CUDA IPC mappings, plain stores).
+    ``exchange="nccl"``: NCCL all-to-all, chunked (`chunks`) to overlap the column transforms.
     """
     P, _ = _world(group)
     if n & (n - 1) or x_local.real.numel() * P != n:
@@ -234,7 +333,10 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
         r1 = N1 // P
         ar = _a2a(xr.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
         ai = _a2a(xi.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
-    zr, zi = _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks)
+    if exchange == "peer" and P <= 8:
+        zr, zi = _four_step_peer(ar.contiguous(), ai.contiguous(), n, group, inverse, natural_order)
+    else:
+        zr, zi = _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks)
     return ComplexTensor(zr, zi)
 
 
