@@ -252,7 +252,8 @@ struct ScatterSpec {
   int npeers;
   float* re[8];
   float* im[8];
-  long long rows, ld, col0;
+  int rows_log;
+  long long ld, col0;
 };
 
 // ld_in / ld_out: floats between consecutive points of one column (default inner).
@@ -270,7 +271,7 @@ static cudaError_t run_axis(const trnfft_plan_s* p, const float* xr, const float
     }
     c.sc_ka = ka;
     c.sc_kb = kb;
-    c.sc_rows = scs->rows;
+    c.sc_rows_log = scs->rows_log;
     c.sc_ld = scs->ld;
     c.sc_col0 = scs->col0;
   };
@@ -799,7 +800,8 @@ int trnfft_exec_fourstep_scatter(trnfft_plan_t plan, trnfft_plan_t tw_plan, cons
   if (npeers < 1 || npeers > 8) return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: 1..8 peers");
   if (plan->logn < 1 || plan->logn > 2 * kMaxColLog || !tw_plan->tw_hi)
     return fail(TRNFFT_UNSUPPORTED, "fourstep_scatter: column length must be a power of two <= 2^20");
-  if (inner < 1 || ld_in < inner || rows_per_peer * npeers != plan->n || peer_ld < peer_col0 + inner)
+  if (inner < 1 || ld_in < inner || rows_per_peer < 1 || rows_per_peer * npeers != plan->n ||
+      peer_ld < peer_col0 + inner)
     return fail(TRNFFT_INVALID_VALUE, "fourstep_scatter: inconsistent sizes");
   int rc = check_ptrs("fourstep_scatter", {in_re, in_im}, 4);
   if (rc) return rc;
@@ -810,7 +812,8 @@ int trnfft_exec_fourstep_scatter(trnfft_plan_t plan, trnfft_plan_t tw_plan, cons
     sc.re[q] = peer_re[q];
     sc.im[q] = peer_im[q];
   }
-  sc.rows = rows_per_peer;
+  sc.rows_log = 0;
+  while ((int64_t(1) << sc.rows_log) < rows_per_peer) ++sc.rows_log;
   sc.ld = peer_ld;
   sc.col0 = peer_col0;
   float* tr = nullptr;

@@ -25,14 +25,22 @@ struct ColGeom {
   static constexpr int LE = 4;
   using S = Sched<LOGL, LE>;
   static constexpr int L = S::N;
-  static constexpr int CT0 = 256 / S::T;
-  static constexpr int CT = CT0 < 8 ? 8 : (CT0 > 64 ? 64 : CT0);
-  static constexpr int THREADS = CT * S::T;
+  static constexpr int T = S::T;  // threads per column
+  // columns per tile: a warp covers 32 (or 16 for L >= 512) neighbouring
+  // columns at one butterfly index, so every global access of a warp is one
+  // contiguous run; small L take several such groups to keep 128+ threads.
+  static constexpr int CW = 32 * T <= 512 ? 32 : 16;
+  static constexpr int G = CW * T >= 128 ? 1 : 128 / (CW * T);
+  static constexpr int CT = CW * G;
+  static constexpr int THREADS = CT * T;
   static constexpr int MINB = THREADS >= 1024 ? 1 : 1024 / THREADS;  // >= 1024 resident threads per SM
-  // column pitch in float2: CT columns of one half-warp land in distinct banks
-  static constexpr int R16 = CT >= 16 ? 1 : 16 / CT;
-  static constexpr int PITCH = S::NP + ((R16 - (S::NP % 16)) + 16) % 16;
-  static constexpr size_t smem = (size_t)CT * PITCH * sizeof(float2);
+  // shared tile [L][CT] of float2 with an odd pitch: a warp's accesses at one
+  // point index are contiguous, and the row-wise read-out (consecutive points
+  // of one column) steps 2*SP banks, conflict-free per half-warp.
+  static constexpr int SP = CT + 1;
+  static constexpr size_t smem_bytes(int kind) {
+    return (S::P > 1 || kind == 1) ? (size_t)L * SP * sizeof(float2) : 0;
+  }
 };
 
 // W_N^e for e already reduced mod N (N = 2^logN <= 2^30): two-level table.
@@ -42,16 +50,35 @@ __device__ __forceinline__ float2 twiddle2(const ColArgs& a, uint32_t e) {
   return make_float2(hi.x * lo.x - hi.y * lo.y, hi.x * lo.y + hi.y * lo.x);
 }
 
+// Stockham passes p .. PLAST-1 of one column through shared memory: on entry
+// (vr, vi) hold pass p's inputs, on return pass PLAST's inputs.  `col` points
+// at the column's first element; point i lives at col[i * SP].
+template <int LOGL, int LE, bool INV, int p, int PLAST, int SP>
+__device__ __forceinline__ void col_mid_passes(int j, float (&vr)[Sched<LOGL, LE>::E],
+                                               float (&vi)[Sched<LOGL, LE>::E], float2* col) {
+  if constexpr (p < PLAST) {
+    if constexpr (p > 0) __syncthreads();  // pass p's inputs have been read by every thread
+    pass_compute_store<LOGL, LE, p, INV>(j, vr, vi, [&](int i, float x, float y) { col[i * SP] = make_float2(x, y); });
+    __syncthreads();
+    pass_load<LOGL, LE, p + 1>(j, vr, vi, [&](int i, float& x, float& y) {
+      const float2 v = col[i * SP];
+      x = v.x;
+      y = v.y;
+    });
+    col_mid_passes<LOGL, LE, INV, p + 1, PLAST, SP>(j, vr, vi, col);
+  }
+}
+
 template <int LOGL, bool INV, int KIND>
 __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k_col(ColArgs a) {
   using GM = ColGeom<LOGL>;
   using S = typename GM::S;
   constexpr int L = GM::L;
   constexpr int CT = GM::CT;
+  constexpr int SP = GM::SP;
   constexpr int THREADS = GM::THREADS;
-  constexpr int ITER = CT * L / THREADS;  // elements per thread in the tile load/store
-  constexpr int RSTEP = THREADS / CT;     // rows advanced per iteration (column-wise mapping)
-  static_assert(THREADS % CT == 0 && (CT * L) % THREADS == 0, "tile mapping");
+  constexpr int PL = S::P - 1;                        // the last Stockham pass
+  constexpr int NSL = 1 << S::logns(PL);              // its output stride
   extern __shared__ float2 sm2[];
   const int tid = threadIdx.x;
   const long long tile = blockIdx.x;
@@ -66,39 +93,30 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   const long long ibase = o1 * a.is_o1 + o2 * a.is_o2 + o3 * a.is_o3;
   const long long obase = o1 * a.os_o1 + o2 * a.os_o2 + o3 * a.os_o3;
 
-  // ---- tile load: thread owns column cl and rows r0 + i*RSTEP; every load is
-  // issued before the first shared-memory store.
+  // thread = (column cl, butterfly lane j); pass 0 reads straight from HBM
   const int cl = tid % CT;
-  const int r0 = tid / CT;
+  const int j = tid / CT;
   const bool colok = c0 + cl < a.ncols;
+  const long long cg = c0 + cl;
+  float vr[S::E], vi[S::E];
   {
-    const long long base = ibase + c0 + cl + (long long)r0 * a.is_j;
-    const float* __restrict__ pr = a.xr + base;
-    const float* __restrict__ pi = a.xi + base;
-    const long long step = (long long)RSTEP * a.is_j;
-    float vr[ITER], vi[ITER];
-#pragma unroll
-    for (int i = 0; i < ITER; ++i) {
-      vr[i] = colok ? __ldg(pr + i * step) : 0.f;
-      vi[i] = colok ? __ldg(pi + i * step) : 0.f;
-    }
-    float2* dst = sm2 + cl * GM::PITCH;
-#pragma unroll
-    for (int i = 0; i < ITER; ++i) dst[spad<S::SH>(r0 + i * RSTEP)] = make_float2(vr[i], vi[i]);
+    const float* __restrict__ pr = a.xr + ibase + cg;
+    const float* __restrict__ pi = a.xi + ibase + cg;
+    const long long is = a.is_j;
+    pass_load<LOGL, GM::LE, 0>(j, vr, vi, [&](int n, float& x, float& y) {
+      x = colok ? __ldg(pr + n * is) : 0.f;
+      y = colok ? __ldg(pi + n * is) : 0.f;
+    });
   }
-  __syncthreads();
-  {
-    const int col = tid / S::T;
-    const int j = tid % S::T;
-    smem_passes<LOGL, GM::LE, INV, 0, S::P>(j, sm2 + col * GM::PITCH);
-  }
+  float2* col = sm2 + cl;
+  col_mid_passes<LOGL, GM::LE, INV, 0, PL, SP>(j, vr, vi, col);
 
-  // ---- twiddle + store.  The exponent for output k of column cg is
-  // e = tw_mul*(o1*(tw_a*cg + tw_b*k) + tw_c*cg*k) = A1*cg + k*(B1 + C1*cg),
-  // evaluated mod 2^32 and then reduced mod N (N divides 2^32).  Along each
-  // thread's sequence of outputs the exponent grows by a fixed step, so the
-  // twiddle is carried by complex multiplication and re-read from the table
-  // every kAnchor outputs (bounded rounding growth, few scattered lookups).
+  // ---- last pass + twiddle + store.  The exponent for output k of column cg
+  // is e = tw_mul*(o1*(tw_a*cg + tw_b*k) + tw_c*cg*k) = A1*cg + k*(B1 + C1*cg),
+  // evaluated mod 2^32 and then reduced mod N (N divides 2^32).  A thread's
+  // outputs of one butterfly are k = b + r*NSL, so the twiddle is carried by
+  // complex multiplication with W^(NSL*de) and re-read from the table every
+  // kAnchor outputs (bounded rounding growth, few scattered lookups).
   constexpr int kAnchor = 8;
   const uint32_t nmask = (uint32_t)a.nmask;
   const long long od = o1 % a.tw_modo;  // the input digit this twiddle multiplies
@@ -113,112 +131,78 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
     if (INV) w.y = -w.y;
     return w;
   };
-  if constexpr (KIND == 2) {
-    // column-wise like kind 0, each output stored into its owner rank's row
-    // buffer (peer memory over NVLink for the other ranks)
-    if (colok) {
-      const long long cg = c0 + cl;
-      const float2* src = sm2 + cl * GM::PITCH;
-      const uint32_t cgt = (uint32_t)(cg + a.tw_coff);
-      const uint32_t de = B1 + C1 * cgt;
-      const uint32_t e0 = A1 * cgt + (uint32_t)r0 * de;
-      float2 w = make_float2(1.f, 0.f), d = w;
-      if (tw) d = look((uint32_t)RSTEP * de);
-#pragma unroll
-      for (int i = 0; i < ITER; ++i) {
-        const int k = r0 + i * RSTEP;
-        float2 v = src[spad<S::SH>(k)];
-        if (tw) {
-          w = (i % kAnchor == 0) ? look(e0 + (uint32_t)i * RSTEP * de) : cmul(w, d);
-          v = cmul(v, w);
-        }
-        const long long K = o1 * a.sc_ka + (long long)k * a.sc_kb;
-        const int q = (int)(K / a.sc_rows);
-        const long long off = (K - (long long)q * a.sc_rows) * a.sc_ld + a.sc_col0 + cg;
-        if (q < a.sc_npeers) {
-          a.sc_re[q][off] = v.x * sc;
-          a.sc_im[q][off] = v.y * sc;
-        }
+  if constexpr (KIND == 0 || KIND == 2) {
+    const uint32_t cgt = (uint32_t)(cg + a.tw_coff);
+    const uint32_t de = B1 + C1 * cgt;
+    const uint32_t ea = A1 * cgt;
+    float2 w = make_float2(1.f, 0.f), d = w;
+    if (tw) d = look((uint32_t)NSL * de);
+    auto twid = [&](int k, int r, float x, float y) {
+      float2 v = make_float2(x, y);
+      if (tw) {
+        w = (r % kAnchor == 0) ? look(ea + (uint32_t)k * de) : cmul(w, d);
+        v = cmul(v, w);
       }
-    }
-    __threadfence_system();
-  } else if constexpr (KIND == 0) {
-    // column-wise, same thread mapping as the load: k = r0 + i*RSTEP
-    if (colok) {
-      const long long cg = c0 + cl;
-      const long long base = obase + cg + (long long)r0 * a.os_k;
-      float* __restrict__ qr = a.yr + base;
-      float* __restrict__ qi = a.yi + base;
-      const long long step = (long long)RSTEP * a.os_k;
-      const float2* src = sm2 + cl * GM::PITCH;
-      const uint32_t cgt = (uint32_t)(cg + a.tw_coff);
-      const uint32_t de = B1 + C1 * cgt;
-      const uint32_t e0 = A1 * cgt + (uint32_t)r0 * de;
-      float2 w = make_float2(1.f, 0.f), d = w;
-      if (tw) d = look((uint32_t)RSTEP * de);
-#pragma unroll
-      for (int i = 0; i < ITER; ++i) {
-        float2 v = src[spad<S::SH>(r0 + i * RSTEP)];
-        if (tw) {
-          w = (i % kAnchor == 0) ? look(e0 + (uint32_t)i * RSTEP * de) : cmul(w, d);
-          v = cmul(v, w);
+      return make_float2(v.x * sc, v.y * sc);
+    };
+    if constexpr (KIND == 0) {
+      float* __restrict__ qr = a.yr + obase + cg;
+      float* __restrict__ qi = a.yi + obase + cg;
+      const long long os = a.os_k;
+      pass_compute_store_r<LOGL, GM::LE, PL, INV>(j, vr, vi, [&](int k, int r, float x, float y) {
+        const float2 v = twid(k, r, x, y);
+        if (colok) {
+          qr[k * os] = v.x;
+          qi[k * os] = v.y;
         }
-        qr[i * step] = v.x * sc;
-        qi[i * step] = v.y * sc;
-      }
+      });
+    } else {
+      // each output goes to its owner rank's row buffer (peer memory over
+      // NVLink for the other ranks): K = o1*ka + k*kb, rank K >> rows_log
+      const long long kbase = o1 * a.sc_ka;
+      const long long rmask = (1LL << a.sc_rows_log) - 1;
+      const long long ccol = a.sc_col0 + cg;
+      pass_compute_store_r<LOGL, GM::LE, PL, INV>(j, vr, vi, [&](int k, int r, float x, float y) {
+        const float2 v = twid(k, r, x, y);
+        const long long K = kbase + (long long)k * a.sc_kb;
+        const int q = (int)(K >> a.sc_rows_log);
+        const long long off = (K & rmask) * a.sc_ld + ccol;
+        if (colok && q < a.sc_npeers) {
+          a.sc_re[q][off] = v.x;
+          a.sc_im[q][off] = v.y;
+        }
+      });
+      __threadfence_system();
     }
   } else {
-    // row-wise: consecutive threads take consecutive k of one column
+    // row-wise (transposing) store: the last pass goes to shared memory, then
+    // consecutive threads take consecutive k of one column
+    if constexpr (PL > 0) __syncthreads();
+    pass_compute_store<LOGL, GM::LE, PL, INV>(j, vr, vi, [&](int i, float x, float y) { col[i * SP] = make_float2(x, y); });
+    __syncthreads();
     float* __restrict__ qr0 = a.yr + obase;
     float* __restrict__ qi0 = a.yi + obase;
-    if constexpr (THREADS <= L) {
-      constexpr int R = L / THREADS;  // k = q*THREADS + tid, columns c = 0..CT-1
+    static_assert(THREADS % L == 0, "row-wise store mapping");
+    constexpr int CPI = THREADS / L;  // columns per iteration; k fixed per thread
+    const int k = tid % L;
+    const int cst = tid / L;
+    const uint32_t mstep = (uint32_t)CPI * (A1 + C1 * (uint32_t)k);
+    float2 w = make_float2(1.f, 0.f), m = w;
+    if (tw) m = look(mstep);
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
-        const int k = q * THREADS + tid;
-        const uint32_t mstep = A1 + C1 * (uint32_t)k;  // exponent step per column
-        const uint32_t coff = (uint32_t)a.tw_coff;
-        float2 w = make_float2(1.f, 0.f), m = w;
-        if (tw) m = look(mstep);
-#pragma unroll
-        for (int c = 0; c < CT; ++c) {
-          const long long cg = c0 + c;
-          if (cg < a.ncols) {
-            float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
-            if (tw) {
-              w = (c % kAnchor == 0)
-                      ? look(A1 * ((uint32_t)cg + coff) + (uint32_t)k * (B1 + C1 * ((uint32_t)cg + coff)))
-                      : cmul(w, m);
-              v = cmul(v, w);
-            }
-            const long long off = cg * a.os_c + k;
-            qr0[off] = v.x * sc;
-            qi0[off] = v.y * sc;
-          }
-        }
+    for (int i = 0; i < CT / CPI; ++i) {
+      const int c = i * CPI + cst;
+      const long long cgc = c0 + c;
+      float2 v = sm2[k * SP + c];
+      if (tw) {
+        const uint32_t cgt = (uint32_t)cgc + (uint32_t)a.tw_coff;
+        w = (i % kAnchor == 0) ? look(A1 * cgt + (uint32_t)k * (B1 + C1 * cgt)) : cmul(w, m);
+        v = cmul(v, w);
       }
-    } else {
-      constexpr int CPI = THREADS / L;  // columns per iteration; k fixed per thread
-      const int k = tid % L;
-      const int cst = tid / L;
-      const uint32_t mstep = (uint32_t)CPI * (A1 + C1 * (uint32_t)k);
-      float2 w = make_float2(1.f, 0.f), m = w;
-      if (tw) m = look(mstep);
-#pragma unroll
-      for (int i = 0; i < ITER; ++i) {
-        const int c = i * CPI + cst;
-        const long long cg = c0 + c;
-        float2 v = sm2[c * GM::PITCH + spad<S::SH>(k)];
-        if (tw) {
-          const uint32_t cgt = (uint32_t)cg + (uint32_t)a.tw_coff;
-          w = (i % kAnchor == 0) ? look(A1 * cgt + (uint32_t)k * (B1 + C1 * cgt)) : cmul(w, m);
-          v = cmul(v, w);
-        }
-        if (cg < a.ncols) {
-          const long long off = cg * a.os_c + k;
-          qr0[off] = v.x * sc;
-          qi0[off] = v.y * sc;
-        }
+      if (cgc < a.ncols) {
+        const long long off = cgc * a.os_c + k;
+        qr0[off] = v.x * sc;
+        qi0[off] = v.y * sc;
       }
     }
   }
@@ -228,8 +212,9 @@ template <int LOGL, bool INV, int KIND>
 static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
   using GM = ColGeom<LOGL>;
   auto kern = k_col<LOGL, INV, KIND>;
-  if (GM::smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
+  constexpr size_t smem = GM::smem_bytes(KIND);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   cudaError_t e0 = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -238,7 +223,7 @@ static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
   const long long tiles = ncb * a.O1 * a.O2 * a.O3;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  kern<<<(unsigned)tiles, GM::THREADS, GM::smem, st>>>(a);
+  kern<<<(unsigned)tiles, GM::THREADS, smem, st>>>(a);
   return cudaGetLastError();
 }
 

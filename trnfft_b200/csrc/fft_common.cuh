@@ -195,11 +195,13 @@ __device__ __forceinline__ void pass_load(int j, float (&vr)[Sched<LOGN, LOGE>::
   }
 }
 
-// Twiddle + in-register DFT + store of pass p.  `st(index, re, im)` receives
-// every output element exactly once.
+// Twiddle + in-register DFT + store of pass p.  `st(index, r, re, im)`
+// receives every output element exactly once; output `index` = base + r*NS,
+// and for each butterfly the calls come in increasing r (r is a compile-time
+// constant after unrolling, so callers may branch on it for free).
 template <int LOGN, int LOGE, int p, bool INV, class St>
-__device__ __forceinline__ void pass_compute_store(int j, float (&vr)[Sched<LOGN, LOGE>::E],
-                                                   float (&vi)[Sched<LOGN, LOGE>::E], St st) {
+__device__ __forceinline__ void pass_compute_store_r(int j, float (&vr)[Sched<LOGN, LOGE>::E],
+                                                     float (&vi)[Sched<LOGN, LOGE>::E], St st) {
   using S = Sched<LOGN, LOGE>;
   constexpr int LR = S::logr(p);
   constexpr int R = 1 << LR;
@@ -246,9 +248,16 @@ __device__ __forceinline__ void pass_compute_store(int j, float (&vr)[Sched<LOGN
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int slot = ct_bitrev(r, LR);
-      st(base + r * NS, ar[slot], ai[slot]);
+      st(base + r * NS, r, ar[slot], ai[slot]);
     }
   }
+}
+
+// As pass_compute_store_r with `st(index, re, im)`.
+template <int LOGN, int LOGE, int p, bool INV, class St>
+__device__ __forceinline__ void pass_compute_store(int j, float (&vr)[Sched<LOGN, LOGE>::E],
+                                                   float (&vi)[Sched<LOGN, LOGE>::E], St st) {
+  pass_compute_store_r<LOGN, LOGE, p, INV>(j, vr, vi, [&](int i, int, float a, float b) { st(i, a, b); });
 }
 
 // Run passes [p, PEND) entirely through shared memory (`sb`: one transform,

@@ -65,12 +65,14 @@ struct ColArgs {
   const float2* tw_lo;
   float scale;
   // kind 2 (scatter to peers): output k of outer block o1 has global index
-  // K = o1*sc_ka + k*sc_kb and goes to rank q = K / sc_rows, row K % sc_rows,
-  // column sc_col0 + c of that rank's row buffer (sc_ld floats per row).
+  // K = o1*sc_ka + k*sc_kb and goes to rank q = K >> sc_rows_log, row
+  // K mod 2^sc_rows_log, column sc_col0 + c of that rank's row buffer (sc_ld
+  // floats per row).
   int sc_npeers;
+  int sc_rows_log;
   float* sc_re[8];
   float* sc_im[8];
-  long long sc_ka, sc_kb, sc_rows, sc_ld, sc_col0;
+  long long sc_ka, sc_kb, sc_ld, sc_col0;
 };
 
 cudaError_t launch_colpass(int logl, bool inv, int kind, const ColArgs& a, cudaStream_t st);
