@@ -159,7 +159,16 @@ static ColArgs col_base(const trnfft_plan_s* p) {
 static constexpr int kMaxColLog = 10;  // column passes transform up to 1024 points on chip
 static constexpr int kMaxMultipassLog = 30;
 
-static constexpr int kMaxDigitLog = 8;  // multi-pass digits of at most 256 points
+// multi-pass digits of at most 2^max_digit_log() points (default 256; the
+// environment variable TRNFFT_B200_MAX_DIGIT_LOG selects 6..10 for tuning)
+static int max_digit_log() {
+  static int v = [] {
+    const char* e = getenv("TRNFFT_B200_MAX_DIGIT_LOG");
+    int d = e ? atoi(e) : 8;
+    return d < 6 ? 6 : (d > kMaxColLog ? kMaxColLog : d);
+  }();
+  return v;
+}
 
 // Contiguous rows of n = 2^p > 4096 points, out of place (in != out).
 // n is split into m digits N_1..N_m (each <= 256 points; n = n_1 + N_1 n_2 +
@@ -174,7 +183,9 @@ static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, c
                                       float* yi, int64_t batch, bool inv, cudaStream_t st) {
   const int L = p->logn;
   const long long N = p->n;
-  const int m = (L + kMaxDigitLog - 1) / kMaxDigitLog;
+  const int md = max_digit_log();
+  const int m0 = (L + md - 1) / md;
+  const int m = m0 > 4 ? 4 : m0;
   if (m < 2 || m > 4) return cudaErrorInvalidValue;
   int lg[5] = {0, 0, 0, 0, 0};  // lg[1..m]
   for (int i = 1; i <= m; ++i) lg[i] = L / m + (i <= L % m ? 1 : 0);

@@ -69,7 +69,15 @@ __device__ __forceinline__ void col_mid_passes(int j, float (&vr)[Sched<LOGL, LE
   }
 }
 
-template <int LOGL, bool INV, int KIND>
+// x / d and x mod d for the tile decode: shift and mask when d = 2^lg
+__device__ __forceinline__ uint32_t qdiv(uint32_t x, uint32_t d, int lg) { return lg >= 0 ? x >> lg : x / d; }
+__device__ __forceinline__ uint32_t qmod(uint32_t x, uint32_t d, int lg) {
+  return lg >= 0 ? x & ((1u << lg) - 1u) : x % d;
+}
+
+// OFF: the integer type of element offsets inside one tile (int when they all
+// fit in 31 bits, which saves the 64-bit multiplies of every access).
+template <int LOGL, bool INV, int KIND, class OFF>
 __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k_col(ColArgs a) {
   using GM = ColGeom<LOGL>;
   using S = typename GM::S;
@@ -81,17 +89,16 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   constexpr int NSL = 1 << S::logns(PL);              // its output stride
   extern __shared__ float2 sm2[];
   const int tid = threadIdx.x;
-  const long long tile = blockIdx.x;
-  const long long ncb = (a.ncols + CT - 1) / CT;
-  const long long cb = tile % ncb;
-  long long rest = tile / ncb;
-  const long long o1 = rest % a.O1;
-  rest /= a.O1;
-  const long long o2 = rest % a.O2;
-  const long long o3 = rest / a.O2;
-  const long long c0 = cb * CT;
-  const long long ibase = o1 * a.is_o1 + o2 * a.is_o2 + o3 * a.is_o3;
-  const long long obase = o1 * a.os_o1 + o2 * a.os_o2 + o3 * a.os_o3;
+  const uint32_t tile = blockIdx.x;
+  const uint32_t cb = qmod(tile, a.d_ncb, a.lg_ncb);
+  uint32_t rest = qdiv(tile, a.d_ncb, a.lg_ncb);
+  const uint32_t o1 = qmod(rest, a.d_O1, a.lg_O1);
+  rest = qdiv(rest, a.d_O1, a.lg_O1);
+  const uint32_t o2 = qmod(rest, a.d_O2, a.lg_O2);
+  const uint32_t o3 = qdiv(rest, a.d_O2, a.lg_O2);
+  const long long c0 = (long long)cb * CT;
+  const long long ibase = (long long)o1 * a.is_o1 + (long long)o2 * a.is_o2 + (long long)o3 * a.is_o3;
+  const long long obase = (long long)o1 * a.os_o1 + (long long)o2 * a.os_o2 + (long long)o3 * a.os_o3;
 
   // thread = (column cl, butterfly lane j); pass 0 reads straight from HBM
   const int cl = tid % CT;
@@ -102,10 +109,10 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   {
     const float* __restrict__ pr = a.xr + ibase + cg;
     const float* __restrict__ pi = a.xi + ibase + cg;
-    const long long is = a.is_j;
+    const OFF is = (OFF)a.is_j;
     pass_load<LOGL, GM::LE, 0>(j, vr, vi, [&](int n, float& x, float& y) {
-      x = colok ? __ldg(pr + n * is) : 0.f;
-      y = colok ? __ldg(pi + n * is) : 0.f;
+      x = colok ? __ldg(pr + (OFF)n * is) : 0.f;
+      y = colok ? __ldg(pi + (OFF)n * is) : 0.f;
     });
   }
   float2* col = sm2 + cl;
@@ -119,7 +126,7 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   // kAnchor outputs (bounded rounding growth, few scattered lookups).
   constexpr int kAnchor = 8;
   const uint32_t nmask = (uint32_t)a.nmask;
-  const long long od = o1 % a.tw_modo;  // the input digit this twiddle multiplies
+  const uint32_t od = qmod(o1, a.d_modo, a.lg_modo);  // the input digit this twiddle multiplies
   const uint32_t A1 = (uint32_t)(a.tw_mul * od * a.tw_a);
   const uint32_t B1 = (uint32_t)(a.tw_mul * od * a.tw_b);
   const uint32_t C1 = (uint32_t)(a.tw_mul * a.tw_c);
@@ -137,36 +144,47 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
     const uint32_t ea = A1 * cgt;
     float2 w = make_float2(1.f, 0.f), d = w;
     if (tw) d = look((uint32_t)NSL * de);
+    const bool scaled = sc != 1.f;
     auto twid = [&](int k, int r, float x, float y) {
       float2 v = make_float2(x, y);
-      if (tw) {
-        w = (r % kAnchor == 0) ? look(ea + (uint32_t)k * de) : cmul(w, d);
+      if (tw) {  // the scale rides on the anchored twiddle
+        if (r % kAnchor == 0) {
+          w = look(ea + (uint32_t)k * de);
+          w.x *= sc;
+          w.y *= sc;
+        } else {
+          w = cmul(w, d);
+        }
         v = cmul(v, w);
+      } else if (scaled) {
+        v.x *= sc;
+        v.y *= sc;
       }
-      return make_float2(v.x * sc, v.y * sc);
+      return v;
     };
     if constexpr (KIND == 0) {
       float* __restrict__ qr = a.yr + obase + cg;
       float* __restrict__ qi = a.yi + obase + cg;
-      const long long os = a.os_k;
+      const OFF os = (OFF)a.os_k;
       pass_compute_store_r<LOGL, GM::LE, PL, INV>(j, vr, vi, [&](int k, int r, float x, float y) {
         const float2 v = twid(k, r, x, y);
         if (colok) {
-          qr[k * os] = v.x;
-          qi[k * os] = v.y;
+          qr[(OFF)k * os] = v.x;
+          qi[(OFF)k * os] = v.y;
         }
       });
     } else {
       // each output goes to its owner rank's row buffer (peer memory over
       // NVLink for the other ranks): K = o1*ka + k*kb, rank K >> rows_log
-      const long long kbase = o1 * a.sc_ka;
-      const long long rmask = (1LL << a.sc_rows_log) - 1;
-      const long long ccol = a.sc_col0 + cg;
+      const OFF kbase = (OFF)o1 * (OFF)a.sc_ka;
+      const OFF rmask = ((OFF)1 << a.sc_rows_log) - 1;
+      const OFF ccol = (OFF)(a.sc_col0 + cg);
+      const OFF kb = (OFF)a.sc_kb, ld = (OFF)a.sc_ld;
       pass_compute_store_r<LOGL, GM::LE, PL, INV>(j, vr, vi, [&](int k, int r, float x, float y) {
         const float2 v = twid(k, r, x, y);
-        const long long K = kbase + (long long)k * a.sc_kb;
+        const OFF K = kbase + (OFF)k * kb;
         const int q = (int)(K >> a.sc_rows_log);
-        const long long off = (K & rmask) * a.sc_ld + ccol;
+        const OFF off = (K & rmask) * ld + ccol;
         if (colok && q < a.sc_npeers) {
           a.sc_re[q][off] = v.x;
           a.sc_im[q][off] = v.y;
@@ -180,8 +198,8 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
     if constexpr (PL > 0) __syncthreads();
     pass_compute_store<LOGL, GM::LE, PL, INV>(j, vr, vi, [&](int i, float x, float y) { col[i * SP] = make_float2(x, y); });
     __syncthreads();
-    float* __restrict__ qr0 = a.yr + obase;
-    float* __restrict__ qi0 = a.yi + obase;
+    float* __restrict__ qr0 = a.yr + obase + c0 * a.os_c;
+    float* __restrict__ qi0 = a.yi + obase + c0 * a.os_c;
     static_assert(THREADS % L == 0, "row-wise store mapping");
     constexpr int CPI = THREADS / L;  // columns per iteration; k fixed per thread
     const int k = tid % L;
@@ -200,7 +218,7 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
         v = cmul(v, w);
       }
       if (cgc < a.ncols) {
-        const long long off = cgc * a.os_c + k;
+        const OFF off = (OFF)c * (OFF)a.os_c + k;
         qr0[off] = v.x * sc;
         qi0[off] = v.y * sc;
       }
@@ -208,10 +226,33 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   }
 }
 
-template <int LOGL, bool INV, int KIND>
-static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
+static int ilog2_exact(long long v) {
+  if (v <= 0 || (v & (v - 1))) return -1;
+  int l = 0;
+  while ((1LL << l) < v) ++l;
+  return l;
+}
+
+// largest element offset a tile touches relative to its base pointers
+template <int LOGL>
+static bool offsets_fit_31(const ColArgs& a, int kind) {
   using GM = ColGeom<LOGL>;
-  auto kern = k_col<LOGL, INV, KIND>;
+  const long long lim = 1LL << 31;
+  const long long L = GM::L, CT = GM::CT;
+  if ((L - 1) * a.is_j + CT >= lim) return false;
+  if (kind == 0 && (L - 1) * a.os_k + CT >= lim) return false;
+  if (kind == 1 && (CT - 1) * a.os_c + L >= lim) return false;
+  if (kind == 2) {
+    const long long kmax = (a.O1 - 1) * a.sc_ka + (L - 1) * a.sc_kb;
+    if (kmax >= lim || (1LL << a.sc_rows_log) * a.sc_ld >= lim || a.sc_col0 + a.ncols >= lim) return false;
+  }
+  return true;
+}
+
+template <int LOGL, bool INV, int KIND, class OFF>
+static cudaError_t launch_col_o(const ColArgs& a, cudaStream_t st) {
+  using GM = ColGeom<LOGL>;
+  auto kern = k_col<LOGL, INV, KIND, OFF>;
   constexpr size_t smem = GM::smem_bytes(KIND);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -223,8 +264,29 @@ static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
   const long long tiles = ncb * a.O1 * a.O2 * a.O3;
   if (tiles <= 0) return cudaSuccess;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  kern<<<(unsigned)tiles, GM::THREADS, smem, st>>>(a);
+  ColArgs b = a;
+  b.d_ncb = (uint32_t)ncb;
+  b.lg_ncb = ilog2_exact(ncb);
+  b.d_O1 = (uint32_t)a.O1;
+  b.lg_O1 = ilog2_exact(a.O1);
+  b.d_O2 = (uint32_t)a.O2;
+  b.lg_O2 = ilog2_exact(a.O2);
+  // o1 mod tw_modo: the identity when tw_modo >= O1
+  if (a.tw_modo >= a.O1) {
+    b.d_modo = 0;
+    b.lg_modo = 31;
+  } else {
+    b.d_modo = (uint32_t)a.tw_modo;
+    b.lg_modo = ilog2_exact(a.tw_modo);
+  }
+  kern<<<(unsigned)tiles, GM::THREADS, smem, st>>>(b);
   return cudaGetLastError();
+}
+
+template <int LOGL, bool INV, int KIND>
+static cudaError_t launch_col_t(const ColArgs& a, cudaStream_t st) {
+  if (offsets_fit_31<LOGL>(a, KIND)) return launch_col_o<LOGL, INV, KIND, int>(a, st);
+  return launch_col_o<LOGL, INV, KIND, long long>(a, st);
 }
 
 template <int LOGL>

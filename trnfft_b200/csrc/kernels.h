@@ -70,6 +70,11 @@ struct ColArgs {
   // floats per row).
   int sc_npeers;
   int sc_rows_log;
+  // filled by launch_colpass: 32-bit tile decode (log2 >= 0 selects shift and
+  // mask for a power of two, else division) and whether every element offset
+  // inside a tile fits in 31 bits
+  uint32_t d_ncb, d_O1, d_O2, d_modo;
+  int lg_ncb, lg_O1, lg_O2, lg_modo;
   float* sc_re[8];
   float* sc_im[8];
   long long sc_ka, sc_kb, sc_ld, sc_col0;
