@@ -398,13 +398,13 @@ class Large(Workload):
             self.step = lambda: D.fft_distributed(x, self.n, natural_order=False, columns_in=True)
             self.launches = {}
             self.no_graph = True
-            self.launches_per_step = 4  # two column passes (the second scatters to the peers) + two row passes
+            self.launches_per_step = 3  # two column passes (the second scatters to the peers) + one row pass
             self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(
                 D.fft_distributed(ComplexTensor(ts[0], ts[1]), self.n, natural_order=False, columns_in=True))
             self.name = (f"single 1-D C2C forward FFT, N=2^{self.logn} across {world} GPUs, four-step with the "
                          "exchange fused into the column kernel (NVLink peer stores) (configs[4])")
             self.dominant = "distributed four-step (column passes with peer-store exchange, row passes)"
-            self.dom_bytes = 2 * 16.0 * self.n / world * 2  # two HBM round trips of the local block (min)
+            self.dom_bytes = 3 * 16.0 * self.n / world  # three passes, each reads and writes the local block
         self.inputs = [self.xr, self.xi]
 
     def check(self, out):

@@ -157,6 +157,7 @@ static ColArgs col_base(const trnfft_plan_s* p) {
 }
 
 static constexpr int kMaxColLog = 10;  // column passes transform up to 1024 points on chip
+static constexpr int kMaxRowBlockLog = 14;  // contiguous rows up to 16384 points in one block
 static constexpr int kMaxMultipassLog = 30;
 
 // multi-pass digits of at most 2^max_digit_log() points (default 256; the
@@ -182,6 +183,11 @@ static int max_digit_log() {
 static cudaError_t run_rows_multipass(const trnfft_plan_s* p, const float* xr, const float* xi, float* yr,
                                       float* yi, int64_t batch, bool inv, cudaStream_t st) {
   const int L = p->logn;
+  if (L <= kMaxRowBlockLog) {
+    // 8192 / 16384 points: one block per transform, one HBM round trip
+    RowArgs a{xr, xi, yr, yi, batch, p->n, p->n, inv ? (float)(1.0 / (double)p->n) : 1.0f};
+    return launch_rows_c2c(L, inv, a, st);
+  }
   const long long N = p->n;
   const int md = max_digit_log();
   const int m0 = (L + md - 1) / md;

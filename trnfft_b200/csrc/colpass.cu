@@ -28,8 +28,11 @@ struct ColGeom {
   static constexpr int T = S::T;  // threads per column
   // columns per tile: a warp covers 32 (or 16 for L >= 512) neighbouring
   // columns at one butterfly index, so every global access of a warp is one
-  // contiguous run; small L take several such groups to keep 128+ threads.
-  static constexpr int CW = 32 * T <= 512 ? 32 : 16;
+  // contiguous 128-byte run (64-byte runs lose up to half the HBM bandwidth
+  // when the rows are a large power of two apart); small L take several such
+  // groups to keep 128+ threads.  Only L = 1024 falls back to 16 columns (a
+  // 32-column tile would not fit in shared memory).
+  static constexpr int CW = 32 * T <= 1024 ? 32 : 16;
   static constexpr int G = CW * T >= 128 ? 1 : 128 / (CW * T);
   static constexpr int CT = CW * G;
   static constexpr int THREADS = CT * T;

@@ -1,5 +1,5 @@
 // Batched power-of-two transforms along contiguous rows, one whole transform
-// per group of threads (single-CTA Stockham, N <= 4096 complex / 8192 real).
+// per group of threads (single-CTA Stockham, N <= 16384 complex / 8192 real).
 //
 // Replaces the reference's per-stage radix-2 loop (trnfft/fft_core.py:53-117)
 // and its NKI Stockham/butterfly kernels (trnfft/nki/stockham.py:55-235,
@@ -221,8 +221,21 @@ constexpr int default_row_variant() {
   return (LOGN == 8 || LOGN == 11) ? 10 : ((LOGN == 9 || LOGN == 10 || LOGN == 12) ? 8 : 0);
 }
 
+// N = 8192 and 16384: one transform per block, E = 32 with 256 / 512 threads
+// (measured 4.0 / 3.2 TB/s on B200 against 3.5 / 2.7 for E = 16 with 512 /
+// 1024 threads, which TRNFFT_B200_ROW_VARIANT=20 selects).
+template <int LOGN, bool INV>
+static cudaError_t launch_c2c_big(const RowArgs& a, cudaStream_t st, int variant) {
+  static_assert(LOGN == 13 || LOGN == 14, "single-block rows up to 16384 points");
+  if (variant == 20) return launch_c2c_v<LOGN, INV, RowVar<4, LOGN == 13 ? 2 : 1, (1 << LOGN) / 16>>(a, st);
+  return launch_c2c_v<LOGN, INV, RowVar<5, LOGN == 13 ? 2 : 1, (1 << LOGN) / 32>>(a, st);
+}
+
 template <int LOGN, bool INV>
 static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st, int variant) {
+  if constexpr (LOGN >= 13) {
+    return launch_c2c_big<LOGN, INV>(a, st, variant);
+  } else {
   if (variant < 0) variant = default_row_variant<LOGN>();
   if constexpr (LOGN >= 8) {
     switch (variant) {
@@ -257,6 +270,7 @@ static cudaError_t launch_c2c_t(const RowArgs& a, cudaStream_t st, int variant) 
     }
   }
   return launch_c2c_v<LOGN, INV, RowVar<4, 1>>(a, st);
+  }
 }
 
 // Real transforms run an M = N/2 point complex FFT: same measured block shapes
@@ -296,6 +310,7 @@ cudaError_t launch_rows_c2c(int logn, bool inv, const RowArgs& a, cudaStream_t s
     TFB_C2C_CASE(1) TFB_C2C_CASE(2) TFB_C2C_CASE(3) TFB_C2C_CASE(4)
     TFB_C2C_CASE(5) TFB_C2C_CASE(6) TFB_C2C_CASE(7) TFB_C2C_CASE(8)
     TFB_C2C_CASE(9) TFB_C2C_CASE(10) TFB_C2C_CASE(11) TFB_C2C_CASE(12)
+    TFB_C2C_CASE(13) TFB_C2C_CASE(14)
     default: return cudaErrorInvalidValue;
   }
 #undef TFB_C2C_CASE

@@ -62,8 +62,15 @@ def _a2a(t: torch.Tensor, group) -> torch.Tensor:
 
 
 def _split_n(n: int) -> tuple[int, int]:
-    l1 = int(math.log2(n)) // 2
-    return 1 << l1, n >> l1
+    """n = N1 * N2: columns of N1 points, rows of N2 <= 16384 points.
+
+    Rows of at most 16384 points are one pass of the row kernel; the column length takes the
+    rest (2^30 = 2^16-point columns, two 256-point column passes, x 2^14-point rows): three
+    HBM passes.
+    """
+    lg = int(math.log2(n))
+    l2 = min(14, lg - lg // 2)
+    return n >> l2, 1 << l2
 
 
 def _twiddle(yr, yi, n, col0, inverse):
@@ -257,8 +264,16 @@ def _device_barrier(group, dev):
     dist.all_reduce(t, group=group)
 
 
-def _four_step_peer(ar, ai, n, group, inverse, natural_order):
-    """CUDA four-step with the exchange inside the column kernel (NVLink peer stores)."""
+_side_streams: dict = {}
+
+
+def _four_step_peer(ar, ai, n, group, inverse, natural_order, chunks=4):
+    """CUDA four-step with the exchange inside the column kernel (NVLink peer stores).
+
+    The column block is cut into `chunks` column ranges issued alternately on two streams, so
+    the NVLink-bound scatter pass of one range overlaps the HBM-bound first column pass of the
+    next.
+    """
     from . import _lib
 
     P, p = _world(group)
@@ -271,11 +286,27 @@ def _four_step_peer(ar, ai, n, group, inverse, natural_order):
         ex = _exchanges[key] = _PeerExchange(n, group, dev)
     plan = _lib.device_plan(N1, dev)
     twp = _lib.device_plan(n, dev)
-    work = torch.empty(2 * N1 * c2, dtype=torch.float32, device=dev) if N1 > 1024 else None
+    nch = chunks if (chunks > 1 and c2 % chunks == 0 and c2 // chunks >= 32) else 1
+    cw = c2 // nch
+    nslab = min(nch, 2)
+    work = torch.empty(nslab, 2 * N1 * cw, dtype=torch.float32, device=dev) if N1 > 1024 else None
+    main = torch.cuda.current_stream(dev)
+    side = _side_streams.get(dev.index)
+    if side is None:
+        side = _side_streams[dev.index] = torch.cuda.Stream(device=dev)
     _device_barrier(group, dev)  # every rank has finished reading its row buffer
-    _lib.call("trnfft_exec_fourstep_scatter", plan.handle, twp.handle, _lib.ptr(ar), _lib.ptr(ai), c2, c2,
-              int(bool(inverse)), p * c2, P, ex.peer_re, ex.peer_im, r1, N2, p * c2, _lib.ptr(work),
-              _lib.stream_ptr(dev))
+    if nch > 1:
+        side.wait_stream(main)
+        for t in (ar, ai) + ((work,) if work is not None else ()):
+            t.record_stream(side)
+    for k in range(nch):
+        st = main if k % 2 == 0 else side
+        wk = _lib.ptr(work[k % nslab]) if work is not None else None
+        _lib.call("trnfft_exec_fourstep_scatter", plan.handle, twp.handle, ar.data_ptr() + 4 * k * cw,
+                  ai.data_ptr() + 4 * k * cw, cw, c2, int(bool(inverse)), p * c2 + k * cw, P, ex.peer_re,
+                  ex.peer_im, r1, N2, p * c2 + k * cw, wk, ctypes.c_void_p(st.cuda_stream))
+    if nch > 1:
+        main.wait_stream(side)
     _device_barrier(group, dev)  # every rank's stores have landed
     zr = torch.empty(r1, N2, dtype=torch.float32, device=dev)
     zi = torch.empty_like(zr)
