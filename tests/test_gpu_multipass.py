@@ -35,6 +35,27 @@ def test_vs_fp64(logn):
     assert rel_l2(cplx(Z), np.fft.ifft(x.astype(np.complex128))) < 2e-6
 
 
+@pytest.mark.parametrize("logn", [13, 14])
+@pytest.mark.parametrize("batch", [1, 3, 150, 300])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_single_block_rows(logn, batch, offset):
+    """Rows of 8192 / 16384 points: the persistent bulk-copy kernel (aligned planes; batches
+    below, at and above the SM count) and the plain kernel (planes offset by one float)."""
+    n = 1 << logn
+    rng = np.random.default_rng(batch + logn)
+    x = (rng.standard_normal((batch, n)) + 1j * rng.standard_normal((batch, n))).astype(np.complex64)
+    br = torch.zeros(batch * n + 1, device="cuda")
+    bi = torch.zeros(batch * n + 1, device="cuda")
+    br[offset:offset + batch * n] = cuda(x.real.reshape(-1))
+    bi[offset:offset + batch * n] = cuda(x.imag.reshape(-1))
+    xr = br[offset:offset + batch * n].view(batch, n)
+    xi = bi[offset:offset + batch * n].view(batch, n)
+    X = trnfft.fft(ComplexTensor(xr, xi))
+    assert rel_l2(cplx(X), np.fft.fft(x.astype(np.complex128))) < 2e-6
+    Z = trnfft.ifft(X)
+    assert rel_l2(cplx(Z), x.astype(np.complex128)) < 2e-6
+
+
 @pytest.mark.parametrize("n", [4096, 65536])
 def test_four_step_vs_reference_golden(golden, n):
     g = golden("four_step")

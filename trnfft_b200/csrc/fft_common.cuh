@@ -200,8 +200,8 @@ __device__ __forceinline__ void pass_load(int j, float (&vr)[Sched<LOGN, LOGE>::
 // and for each butterfly the calls come in increasing r (r is a compile-time
 // constant after unrolling, so callers may branch on it for free).
 template <int LOGN, int LOGE, int p, bool INV, class St>
-__device__ __forceinline__ void pass_compute_store_r(int j, float (&vr)[Sched<LOGN, LOGE>::E],
-                                                     float (&vi)[Sched<LOGN, LOGE>::E], St st) {
+__device__ __forceinline__ void pass_compute_store_qr(int j, float (&vr)[Sched<LOGN, LOGE>::E],
+                                                      float (&vi)[Sched<LOGN, LOGE>::E], St st) {
   using S = Sched<LOGN, LOGE>;
   constexpr int LR = S::logr(p);
   constexpr int R = 1 << LR;
@@ -248,8 +248,35 @@ __device__ __forceinline__ void pass_compute_store_r(int j, float (&vr)[Sched<LO
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int slot = ct_bitrev(r, LR);
-      st(base + r * NS, r, ar[slot], ai[slot]);
+      st(base + r * NS, q * R + r, r, ar[slot], ai[slot]);
     }
+  }
+}
+
+// st(index, r, re, im); `pass_compute_store_qr` also passes the register
+// slot q*R + r the value came from, so callers can keep outputs in (vr, vi).
+template <int LOGN, int LOGE, int p, bool INV, class St>
+__device__ __forceinline__ void pass_compute_store_r(int j, float (&vr)[Sched<LOGN, LOGE>::E],
+                                                     float (&vi)[Sched<LOGN, LOGE>::E], St st) {
+  pass_compute_store_qr<LOGN, LOGE, p, INV>(j, vr, vi,
+                                            [&](int i, int, int r, float a, float b) { st(i, r, a, b); });
+}
+
+// Index of the output held in register slot q*R + r after pass p.
+template <int LOGN, int LOGE, int p, class F>
+__device__ __forceinline__ void pass_outputs(int j, F f) {
+  using S = Sched<LOGN, LOGE>;
+  constexpr int LR = S::logr(p);
+  constexpr int R = 1 << LR;
+  constexpr int Q = S::E / R;
+  constexpr int LNS = S::logns(p);
+  constexpr int NS = 1 << LNS;
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    const int b = j + q * S::T;
+    const int base = ((b >> LNS) << (LNS + LR)) + (b & (NS - 1));
+#pragma unroll
+    for (int r = 0; r < R; ++r) f(q * R + r, base + r * NS);
   }
 }
 
