@@ -57,9 +57,10 @@ __global__ void __launch_bounds__(StftGeom<LOGM>::THREADS, StftGeom<LOGM>::MINB)
   extern __shared__ float2 sm2[];
   const int g = threadIdx.x / S::T;
   const int j = threadIdx.x % S::T;
-  const long long nfb = (a.frames + GM::G - 1) / GM::G;
+  // block -> (waveform, frame group) in 32-bit arithmetic (blocks < 2^31)
+  const uint32_t nfb = (uint32_t)((a.frames + GM::G - 1) / GM::G);
   const long long b = blockIdx.x / nfb;
-  const long long f0 = (blockIdx.x % nfb) * GM::G;
+  const long long f0 = (long long)(blockIdx.x % nfb) * GM::G;
   const long long f = f0 + g;
   const bool valid = f < a.frames;
   const float* __restrict__ x = a.x + b * a.len;
