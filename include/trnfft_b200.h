@@ -56,7 +56,7 @@ typedef enum {
 typedef enum {
   TRNFFT_ALG_COPY = 0,      /* n == 1 */
   TRNFFT_ALG_STOCKHAM = 1,  /* power of two, n <= 4096: one pass over HBM */
-  TRNFFT_ALG_MULTIPASS = 2, /* power of two, n > 4096: 2-3 passes over HBM */
+  TRNFFT_ALG_MULTIPASS = 2, /* power of two, n > 4096: one pass up to 16384, else 2-4 passes */
   TRNFFT_ALG_BLUESTEIN = 3  /* any other n: fused chirp-z, one pass over HBM */
 } trnfft_algorithm;
 
@@ -95,7 +95,8 @@ TRNFFT_API int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* pa
  * Replaces fft_core(x, inverse) (trnfft/fft_core.py:22-50) -> _cooley_tukey
  * (fft_core.py:53-117) / _bluestein (fft_core.py:1285-1376), reached from
  * trnfft.fft / trnfft.ifft (trnfft/api.py:22-35).
- * Power-of-two n > 4096 (up to 2^30) run as two or three column-tile passes
+ * Power-of-two 4096 < n <= 16384 run as one row pass (one transform per
+ * block); larger n (up to 2^30) as two to four column-tile passes
  * (four-step / six-step, trnfft/nki/multicore.py:151-219).  In-place calls
  * (in == out) are allowed; for n > 4096 they need `work`, a device buffer
  * of trnfft_plan_query's work_bytes; out-of-place calls need none (NULL). */
