@@ -14,7 +14,10 @@
   5. length-N2 transforms along the rows
   The result is X[k1 + N1*k2] for k1 in block p ("transposed" distribution).  With
   ``natural_order=True`` a third all-to-all returns the contiguous chunk
-  X[p N/P : (p+1) N/P] to rank p.
+  X[p N/P : (p+1) N/P] to rank p.  On one node (``exchange="peer"``, the default) steps 3
+  and 4 happen inside the last column pass: it stores each twiddled output straight into the
+  owning rank's row buffer over NVLink (CUDA IPC mappings), and one-element all-reduces order
+  the ranks before and after it.  Rows have at most 16384 points (one row-kernel pass).
 * ``fft2_distributed``: rows of a 2-D field sharded across ranks; row transforms, one
   all-to-all transpose, column transforms (output in column-block layout, or row layout again
   with ``natural_order=True``).
