@@ -81,7 +81,8 @@ __device__ __forceinline__ uint32_t qmod(uint32_t x, uint32_t d, int lg) {
 // OFF: the integer type of element offsets inside one tile (int when they all
 // fit in 31 bits, which saves the 64-bit multiplies of every access).
 template <int LOGL, bool INV, int KIND, class OFF>
-__global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k_col(ColArgs a) {
+__device__ __forceinline__ void col_tile(const ColArgs& a, const uint32_t tile, float* const* s_re,
+                                         float* const* s_im) {
   using GM = ColGeom<LOGL>;
   using S = typename GM::S;
   constexpr int L = GM::L;
@@ -92,7 +93,6 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
   constexpr int NSL = 1 << S::logns(PL);              // its output stride
   extern __shared__ float2 sm2[];
   const int tid = threadIdx.x;
-  const uint32_t tile = blockIdx.x;
   const uint32_t cb = qmod(tile, a.d_ncb, a.lg_ncb);
   uint32_t rest = qdiv(tile, a.d_ncb, a.lg_ncb);
   const uint32_t o1 = qmod(rest, a.d_O1, a.lg_O1);
@@ -189,11 +189,10 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
         const int q = (int)(K >> a.sc_rows_log);
         const OFF off = (K & rmask) * ld + ccol;
         if (colok && q < a.sc_npeers) {
-          a.sc_re[q][off] = v.x;
-          a.sc_im[q][off] = v.y;
+          s_re[q][off] = v.x;
+          s_im[q][off] = v.y;
         }
       });
-      __threadfence_system();
     }
   } else {
     // row-wise (transposing) store: the last pass goes to shared memory, then
@@ -227,6 +226,25 @@ __global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k
       }
     }
   }
+}
+
+// One tile per iteration; the grid is the tile count unless ColArgs.max_blocks
+// caps it (the scatter pass then leaves SMs to a concurrent kernel).
+template <int LOGL, bool INV, int KIND, class OFF>
+__global__ void __launch_bounds__(ColGeom<LOGL>::THREADS, ColGeom<LOGL>::MINB) k_col(ColArgs a) {
+  __shared__ float* s_ptr[16];  // kind 2: the peers' row buffers, re then im
+  if constexpr (KIND == 2) {
+    if (threadIdx.x < (unsigned)a.sc_npeers) {
+      s_ptr[threadIdx.x] = a.sc_re[threadIdx.x];
+      s_ptr[8 + threadIdx.x] = a.sc_im[threadIdx.x];
+    }
+    __syncthreads();
+  }
+  for (uint32_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x) {
+    col_tile<LOGL, INV, KIND, OFF>(a, tile, s_ptr, s_ptr + 8);
+    if (tile + gridDim.x < a.ntiles) __syncthreads();  // the tile's shared memory is free again
+  }
+  if constexpr (KIND == 2) __threadfence_system();
 }
 
 static int ilog2_exact(long long v) {
@@ -282,7 +300,10 @@ static cudaError_t launch_col_o(const ColArgs& a, cudaStream_t st) {
     b.d_modo = (uint32_t)a.tw_modo;
     b.lg_modo = ilog2_exact(a.tw_modo);
   }
-  kern<<<(unsigned)tiles, GM::THREADS, smem, st>>>(b);
+  b.ntiles = (uint32_t)tiles;
+  long long grid = tiles;
+  if (a.max_blocks > 0 && a.max_blocks < grid) grid = a.max_blocks;
+  kern<<<(unsigned)grid, GM::THREADS, smem, st>>>(b);
   return cudaGetLastError();
 }
 

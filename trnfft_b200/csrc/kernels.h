@@ -75,6 +75,8 @@ struct ColArgs {
   // inside a tile fits in 31 bits
   uint32_t d_ncb, d_O1, d_O2, d_modo;
   int lg_ncb, lg_O1, lg_O2, lg_modo;
+  uint32_t ntiles;   // filled by launch_colpass
+  long long max_blocks;  // > 0: cap on the grid (tiles loop), 0: one block per tile
   float* sc_re[8];
   float* sc_im[8];
   long long sc_ka, sc_kb, sc_ld, sc_col0;

@@ -270,12 +270,13 @@ def _device_barrier(group, dev):
 _side_streams: dict = {}
 
 
-def _four_step_peer(ar, ai, n, group, inverse, natural_order, chunks=4):
+def _four_step_peer(ar, ai, n, group, inverse, natural_order, chunks=1):
     """CUDA four-step with the exchange inside the column kernel (NVLink peer stores).
 
-    The column block is cut into `chunks` column ranges issued alternately on two streams, so
-    the NVLink-bound scatter pass of one range overlaps the HBM-bound first column pass of the
-    next.
+    With `chunks` > 1 the column block is cut into column ranges issued alternately on two
+    streams (the scatter pass of one range next to the first pass of the next); on B200 this
+    measured no faster than one range (2 GPUs, 2^30: 7.58-7.64 ms either way), so one range
+    is the default.
     """
     from . import _lib
 
@@ -341,7 +342,8 @@ def column_block(x_full_re: torch.Tensor, x_full_im: torch.Tensor, n: int, world
 
 
 def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natural_order: bool = True,
-                    group=None, columns_in: bool = False, chunks: int = 4, exchange: str = "peer") -> ComplexTensor:
+                    group=None, columns_in: bool = False, chunks: int | None = None,
+                    exchange: str = "peer") -> ComplexTensor:
     """Distributed 1-D FFT of length n = 2^k.
 
     Rank p passes its contiguous chunk of n/P points, or with ``columns_in`` its column block
@@ -349,8 +351,10 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
     chunk of X (``natural_order``) or X[k1 + N1*k2] for k1 in block p stored [k1][k2].
 
     ``exchange="peer"`` (default, one node): the column kernel stores its output straight into
-    the owning ranks' row buffers over NVLink (CUDA IPC mappings, plain stores).
-    ``exchange="nccl"``: NCCL all-to-all, chunked (`chunks`) to overlap the column transforms.
+    the owning ranks' row buffers over NVLink (CUDA IPC mappings, plain stores); ``chunks``
+    (default 1) column ranges on two streams.
+    ``exchange="nccl"``: NCCL all-to-all, chunked (``chunks``, default 4) to overlap the column
+    transforms.
     """
     P, _ = _world(group)
     if n & (n - 1) or x_local.real.numel() * P != n:
@@ -368,9 +372,10 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
         ar = _a2a(xr.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
         ai = _a2a(xi.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
     if exchange == "peer" and P <= 8:
-        zr, zi = _four_step_peer(ar.contiguous(), ai.contiguous(), n, group, inverse, natural_order)
+        zr, zi = _four_step_peer(ar.contiguous(), ai.contiguous(), n, group, inverse, natural_order,
+                                 chunks=1 if chunks is None else chunks)
     else:
-        zr, zi = _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks)
+        zr, zi = _four_step_overlapped(ar, ai, n, group, inverse, natural_order, 4 if chunks is None else chunks)
     return ComplexTensor(zr, zi)
 
 
