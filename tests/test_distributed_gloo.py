@@ -108,3 +108,18 @@ def test_shard_rows_cover_everything():
             spans = [shard_rows(total, world, r) for r in range(world)]
             assert spans[0][0] == 0 and spans[-1][1] == total
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+def test_split_n():
+    """Rows of at most 16384 points (one row-kernel pass); the columns take the rest."""
+    from trnfft_b200.distributed import _split_n
+
+    assert _split_n(1 << 30) == (1 << 16, 1 << 14)
+    assert _split_n(1 << 28) == (1 << 14, 1 << 14)
+    assert _split_n(4096) == (64, 64)
+    assert _split_n(1 << 13) == (64, 128)
+    for lg in range(2, 33):
+        n1, n2 = _split_n(1 << lg)
+        assert n1 * n2 == 1 << lg
+        assert n2 <= 1 << 14
+        assert n2 >= n1 or n2 == 1 << 14
