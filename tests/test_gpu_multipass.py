@@ -179,3 +179,37 @@ def test_axis_with_fused_four_step_twiddle(n1, cols, col0, big, inverse):
     e = (k * c) % big
     w = np.exp((2j if inverse else -2j) * np.pi * e / big)
     assert rel_l2(host(yr) + 1j * host(yi), f * w) < 2e-6
+
+
+@pytest.mark.parametrize("n1,work_needed", [(512, False), (1 << 16, True)])
+@pytest.mark.parametrize("inverse", [False, True])
+@pytest.mark.parametrize("cap", [None, "7"])
+def test_fourstep_scatter_one_gpu(monkeypatch, n1, work_needed, inverse, cap):
+    """trnfft_exec_fourstep_scatter with two row buffers on one GPU: output row K of the twiddled
+    column FFT lands in buffer K // rows_per_peer, row K % rows_per_peer, columns peer_col0 + c.
+    cap: TRNFFT_B200_SCATTER_BLOCKS (7 blocks loop over every tile)."""
+    if cap is not None:
+        monkeypatch.setenv("TRNFFT_B200_SCATTER_BLOCKS", cap)
+    cols, big, col_offset, peer_col0, peer_ld = 64, 1 << 26, 192, 64, 160
+    rpp = n1 // 2
+    rng = np.random.default_rng(n1 + int(inverse))
+    x = (rng.standard_normal((n1, cols)) + 1j * rng.standard_normal((n1, cols))).astype(np.complex64)
+    xr, xi = cuda(x.real), cuda(x.imag)
+    bufs = [torch.zeros(rpp, peer_ld, device="cuda") for _ in range(4)]  # re0, re1, im0, im1
+    pre = (ctypes.c_void_p * 2)(bufs[0].data_ptr(), bufs[1].data_ptr())
+    pim = (ctypes.c_void_p * 2)(bufs[2].data_ptr(), bufs[3].data_ptr())
+    work = torch.empty(2 * n1 * cols, device="cuda") if work_needed else None
+    plan = _lib.device_plan(n1, xr.device)
+    twp = _lib.device_plan(big, xr.device)
+    _lib.call("trnfft_exec_fourstep_scatter", plan.handle, twp.handle, _lib.ptr(xr), _lib.ptr(xi), cols, cols,
+              int(inverse), col_offset, 2, pre, pim, rpp, peer_ld, peer_col0, _lib.ptr(work),
+              _lib.stream_ptr(xr.device))
+    xd = x.astype(np.complex128)
+    f = np.fft.ifft(xd, axis=0) if inverse else np.fft.fft(xd, axis=0)
+    k = np.arange(n1)[:, None]
+    c = np.arange(cols)[None, :] + col_offset
+    y = f * np.exp((2j if inverse else -2j) * np.pi * ((k * c) % big) / big)
+    got = np.concatenate([host(bufs[q]) + 1j * host(bufs[2 + q]) for q in range(2)], axis=0)
+    assert rel_l2(got[:, peer_col0:peer_col0 + cols], y) < 2e-6
+    untouched = np.concatenate([got[:, :peer_col0], got[:, peer_col0 + cols:]], axis=1)
+    assert not untouched.any()
