@@ -24,7 +24,9 @@ struct StftGeom {
   static constexpr int G = G0 < 1 ? 1 : G0;  // frames per block
   static constexpr int THREADS = G * S::T;
   static constexpr int MINB = THREADS >= 1024 ? 1 : 1024 / THREADS;
-  static constexpr int FP = S::NP + 1;  // odd pitch: frame-strided smem reads avoid bank conflicts
+  // frame pitch = 2 (mod 16) float2: in the split read-out a half-warp covers 8 frames x 2
+  // neighbouring bins, which then fall on 16 distinct bank pairs
+  static constexpr int FP = S::NP + ((2 - S::NP % 16) + 16) % 16;
   static constexpr size_t smem = (size_t)G * FP * sizeof(float2);
 };
 
