@@ -2,13 +2,15 @@
 // transforms and of transforms along a strided axis (fft2 / fftn).
 //
 // A tile is CT neighbouring "columns" (unit stride in HBM) of L-point
-// transforms whose points are `is_j` floats apart.  The block loads the tile
-// with coalesced reads (CT consecutive floats per point), keeps each column
-// as one padded float2 transform in shared memory, runs every Stockham pass
-// of the L-point FFT on chip, applies an optional twiddle W_N^e, and stores
-// the tile either column-wise again (KIND 0, in place allowed) or row-wise
-// (KIND 1: column c becomes a contiguous run of L outputs, which is the
-// transposition step of the four-step / six-step algorithm).
+// transforms whose points are `is_j` floats apart.  Thread (column, lane)
+// loads its first-pass inputs straight from HBM (a warp reads one contiguous
+// run of 32 columns per point), the middle Stockham passes exchange through
+// a shared [L][CT+1] tile, and the last pass applies an optional twiddle
+// W_N^e in registers and stores either column-wise (KIND 0, in place
+// allowed), into the owning rank's row buffer (KIND 2, the four-step exchange
+// over NVLink), or row-wise through shared memory (KIND 1: column c becomes a
+// contiguous run of L outputs, the transposition step of the four-step /
+// six-step algorithm).
 //
 // Four-step reference: trnfft/nki/multicore.py:151-219 (column DFTs, twiddle
 // exp(sign*2*pi*i*l*k1/N), row DFTs, column-major flatten), which runs the
