@@ -203,6 +203,12 @@ class Workload:
     unit = UNIT
     dominant = None
 
+    def release(self):
+        """Drop the device inputs (the default run frees them before its extras)."""
+        for k in ("xr", "xi", "xs", "x", "inputs", "step", "launches", "e2e_fn"):
+            if hasattr(self, k):
+                setattr(self, k, None)
+
     def cpu_sample(self, threads):
         raise NotImplementedError
 
@@ -238,6 +244,14 @@ class C2CRoundTrip(Workload):
 
     def check(self, out):
         return rel_err(out.real, self.xr)
+
+    def ref_full_units(self):
+        return self.batch
+
+    def ref_sample(self, T, units):
+        g = torch.Generator().manual_seed(0)
+        x = T.ComplexTensor(torch.randn(units, self.n, generator=g), torch.randn(units, self.n, generator=g))
+        return (lambda: T.ifft(T.fft(x))), 2 * c2c_flops(self.n, units), f"{units} of {self.batch} rows"
 
     def cpu_sample(self, threads, rows):
         from oracle import trnfft_oracle as O
@@ -292,6 +306,16 @@ class SmallN(Workload):
         ref = torch.fft.fft(torch.complex(x.real, x.imag))
         return rel_err(torch.complex(out.real, out.imag), ref)
 
+    def ref_full_units(self):
+        return self.batch
+
+    def ref_sample(self, T, units):
+        g = torch.Generator().manual_seed(0)
+        xs = [T.ComplexTensor(torch.randn(units, n, generator=g), torch.randn(units, n, generator=g))
+              for n in self.ns]
+        return ((lambda: [T.fft(x) for x in xs]), sum(c2c_flops(n, units) for n in self.ns),
+                f"{units} of {self.batch} rows for each N")
+
     def cpu_sample(self, threads, rows):
         from oracle import trnfft_oracle as O
 
@@ -344,6 +368,16 @@ class Stft(Workload):
                          return_complex=True)
         return rel_err(torch.complex(out.real[:8], out.imag[:8]), ref)
 
+    def ref_full_units(self):
+        return self.B
+
+    def ref_sample(self, T, units):
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(units, self.L, generator=g)
+        win = torch.hann_window(self.nfft)
+        return ((lambda: T.stft(x, self.nfft, self.hop, window=win)), float(units * self.frames),
+                f"{units} of {self.B} waveforms")
+
     def cpu_sample(self, threads, rows):
         from oracle import trnfft_oracle as O
 
@@ -381,13 +415,24 @@ class Large(Workload):
         world = int(os.environ.get("WORLD_SIZE", "1"))
         self.world = world
         if world == 1:
-            self.xr = torch.randn(1, self.n, device=dev, generator=g)
-            self.xi = torch.randn(1, self.n, device=dev, generator=g)
+            from trnfft_b200 import distributed as D
+
+            # the same four-step split as the multi-GPU run (2^16-point columns x 2^14-point
+            # rows, transposed output order): three HBM passes on one GPU
+            N1, N2 = D._split_n(self.n)
+            self.xr = torch.randn(N1, N2, device=dev, generator=g)
+            self.xi = torch.randn(N1, N2, device=dev, generator=g)
             x = ComplexTensor(self.xr, self.xi)
-            self.step = lambda: trnfft.fft(x)
+            self.step = lambda: D.fft_four_step_local(x, self.n)
             self.launches = {"fft": self.step}
-            self.launches_per_step = 4
-            self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(trnfft.fft(ComplexTensor(ts[0], ts[1])))
+            self.launches_per_step = 3
+            self.dom_bytes = 3 * 16.0 * self.n
+            self.dominant = "four-step on one GPU: two column passes (twiddle fused) + one 16384-point row pass"
+            self.name = (f"single 1-D C2C forward FFT, N=2^{self.logn}, four-step 2^16 x 2^14 on one GPU, "
+                         "transposed output order (configs[4])")
+            self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(
+                D.fft_four_step_local(ComplexTensor(ts[0], ts[1]), self.n))
+            self.natural = lambda: trnfft.fft(ComplexTensor(self.xr.reshape(1, -1), self.xi.reshape(1, -1)))
         else:
             from trnfft_b200 import distributed as D
 
@@ -406,6 +451,17 @@ class Large(Workload):
             self.dominant = "distributed four-step (column passes with peer-store exchange, row passes)"
             self.dom_bytes = 3 * 16.0 * self.n / world  # three passes, each reads and writes the local block
         self.inputs = [self.xr, self.xi]
+
+    def ref_sample(self, T, units):
+        from trnfft.nki.multicore import _stage_parallel_fft
+
+        n = 1 << 20
+        g = torch.Generator().manual_seed(0)
+        x = T.ComplexTensor(torch.randn(n, generator=g), torch.randn(n, generator=g))
+        return ((lambda: _stage_parallel_fft(x, 1, False)), c2c_flops(n, 1),
+                "one N=2^20 transform through the reference's four-step _stage_parallel_fft")
+
+    ref_fixed_units = True
 
     def check(self, out):
         # Parseval over all ranks: sum |X|^2 = N sum |x|^2
@@ -460,6 +516,14 @@ class Fft2(Workload):
         ref = torch.fft.fft2(torch.complex(self.xr, self.xi))
         return rel_err(torch.complex(out.real, out.imag), ref)
 
+    def ref_sample(self, T, units):
+        s_ = 1024
+        g = torch.Generator().manual_seed(0)
+        x = T.ComplexTensor(torch.randn(s_, s_, generator=g), torch.randn(s_, s_, generator=g))
+        return (lambda: T.fft2(x)), 2 * c2c_flops(s_, s_), "one 1024x1024 fft2"
+
+    ref_fixed_units = True
+
     def cpu_sample(self, threads, rows):
         from oracle import trnfft_oracle as O
 
@@ -501,6 +565,23 @@ class LinearWL(Workload):
         self.launches_per_step = 6  # 4 split kernels + 2 GEMMs
         self.inputs = [self.xr, self.xi]
         self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(self.layer(ComplexTensor(ts[0], ts[1])))
+
+    def ref_full_units(self):
+        return self.M
+
+    def ref_sample(self, T, units):
+        import trnfft.nn as TN
+
+        torch.manual_seed(77)
+        layer = TN.ComplexLinear(self.K, self.N, bias=True)
+        g = torch.Generator().manual_seed(0)
+        x = T.ComplexTensor(torch.randn(units, self.K, generator=g), torch.randn(units, self.K, generator=g))
+
+        def f():
+            with torch.no_grad():
+                return layer(x)
+
+        return f, 8.0 * units * self.N * self.K, f"{units} of {self.M} rows"
 
     def check(self, out):
         w_r, w_i = self.layer.W_re.weight, self.layer.W_im.weight
@@ -584,12 +665,81 @@ def scale_value(v, unit):
     return v / 1e9 if unit == UNIT else v
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def import_reference():
+    """The unmodified reference package installed in baseline/_ref, on its own CPU
+    ('pytorch') backend, or None when it is not installed."""
+    if not os.path.isdir(os.path.join(REF_DIR, "trnfft")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import trnfft as T
+
+    T.set_backend("pytorch")
+    T.set_precision("fast")
+    return T
+
+
+def calibrate_units(wl, T, target_s):
+    """Largest sample (rows / waveforms, growing 4x up to the full workload) whose reference
+    step stays within target_s.  The reference's per-call cost is mostly a fixed Python loop
+    over butterfly stages, so larger samples are much cheaper per row."""
+    if getattr(wl, "ref_fixed_units", False):
+        return 1
+    full = wl.ref_full_units()
+    units, best = 4, None
+    while True:
+        fn, _, _ = wl.ref_sample(T, units)
+        t0 = time.perf_counter()
+        fn()
+        dt = time.perf_counter() - t0
+        if dt > target_s and best is not None:
+            return best
+        best = units
+        if dt > target_s or units >= full:
+            return best
+        units = min(full, units * 4)
+
+
+def time_reference(wl, T, steps, warmup, target_s=5.0):
+    """Time `steps` reference steps (each one bounded sample of the workload) with
+    perf_counter; returns (rate per second, mean s per step, sample description)."""
+    units = calibrate_units(wl, T, target_s)
+    fn, work, desc = wl.ref_sample(T, units)
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    mean = sum(ts) / len(ts)
+    return work / mean, mean, desc
+
+
 def cpu_baseline(wl, budget_s):
+    """Reported CPU baseline: the reference itself (baseline/_ref) when installed, plus the
+    NumPy port of its algorithm (oracle/trnfft_oracle.py) as a second entry."""
     threads = os.cpu_count() or 1
-    rate, t, reps = cpu_rate(wl, threads, budget_s)
-    return {"value": round(scale_value(rate, wl.unit), 4), "unit": wl.unit, "cores": threads, "kind": "port",
+    out = {}
+    T = import_reference()
+    if T is not None:
+        torch.set_num_threads(threads)
+        steps = 3
+        rate, mean, desc = time_reference(wl, T, steps, 1, target_s=min(2.0, budget_s / (steps + 3)))
+        out = {"value": round(scale_value(rate, wl.unit), 4), "unit": wl.unit, "cores": threads,
+               "kind": "reference",
+               "sample": f"trnfft (baseline/_ref, backend 'pytorch', {threads} torch threads): {desc} per step, "
+                         f"{steps} steps of {mean:.2f} s"}
+    rate, t, reps = cpu_rate(wl, threads, budget_s / 2 if T is not None else budget_s)
+    port = {"value": round(scale_value(rate, wl.unit), 4), "unit": wl.unit, "cores": threads, "kind": "port",
             "sample": f"oracle/trnfft_oracle.py ({wl.name}), {reps} bounded sample(s) in {t:.1f} s "
                       f"on {threads} host threads"}
+    if not out:
+        return port, None
+    return out, port
 
 
 def run_reference(args, world, rank):
@@ -597,25 +747,37 @@ def run_reference(args, world, rank):
         return
     wl = make_workload(args)
     threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        wl.cpu_sample(threads, 64)
-    times, works = [], []
-    for _ in range(args.steps):
-        t, w = wl.cpu_sample(threads, 256)
-        times.append(t)
-        works.append(w)
-    rate = sum(works) / sum(times)
+    T = import_reference()
+    if T is not None:
+        torch.set_num_threads(threads)
+        rate, mean, desc = time_reference(wl, T, args.steps, args.warmup)
+        kind = "reference"
+        sample = (f"trnfft {getattr(T, '__version__', '')} from baseline/_ref, backend 'pytorch', "
+                  f"{threads} torch threads; each step = {desc}")
+    else:
+        # the reference is not installed: its algorithm restated in NumPy (oracle port)
+        units = 256
+        for _ in range(args.warmup):
+            wl.cpu_sample(threads, 64)
+        ts, works = [], []
+        for _ in range(args.steps):
+            t, w = wl.cpu_sample(threads, units)
+            ts.append(t)
+            works.append(w)
+        rate, mean = sum(works) / sum(ts), sum(ts) / len(ts)
+        kind = "port"
+        sample = f"oracle/trnfft_oracle.py (the reference's algorithm in NumPy), {units} rows per step"
     value = round(scale_value(rate, wl.unit), 4)
     out = {
         "impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1000.0 * wl.work / rate, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1000.0 * mean, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl.name + "; each step times a bounded sample and reports the rate",
+        "config": {"workload": wl.name + f"; reference CPU path, each step = {sample}",
                    "parallelism": f"{threads} host threads"},
-        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": "port",
-                         "sample": "bounded sample per step, oracle/trnfft_oracle.py (the reference's algorithm)"},
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "timing": "time.perf_counter around each step; ms_per_step is the measured mean step time",
     }
     print(json.dumps(out), flush=True)
 
@@ -709,6 +871,8 @@ def run_ours(args, world, rank, local):
     dev_in = [torch.empty_like(t) for t in wl.inputs]
     outs = wl.e2e_fn(dev_in)
     host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in)
+    d2h_bytes = sum(t.numel() * t.element_size() for t in host_out)
 
     def e2e_step():
         for d, h in zip(dev_in, host_in):
@@ -730,6 +894,15 @@ def run_ours(args, world, rank, local):
     barrier(world)
     e2e_max = allreduce_max(sum(e2e_ms) / len(e2e_ms), world)
     e2e_value = (1 if strong else world) * wl.work / (e2e_max / 1e3)
+
+    extras = {}
+    if args.extras and args.workload == "c2c1024" and not args.size:
+        del dev_in, host_in, host_out, outs
+        wl.release()
+        torch.cuda.empty_cache()
+        if world > 1:
+            extras["multi_gpu_check_rel_l2"] = multi_gpu_check(world, rank, dev)
+        extras["large_four_step"] = large_extra(world, rank, dev)
 
     if rank != 0:
         return
@@ -761,16 +934,143 @@ def run_ours(args, world, rank, local):
                      "algorithmic_bytes_per_launch": wl.dom_bytes, "avg_launch_ms": round(avg_launch, 5)},
         "e2e": {"value": round(scale_value(e2e_value, wl.unit), 3), "unit": wl.unit,
                 "ms_per_step": round(e2e_max, 4),
-                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
-                "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out)},
+                "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes},
         "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk.summary(),
         "check_rel_l2": err, "parity_ok": bool(err < 1e-5),
         "timing": "CUDA events around CUDA-graph replays of the step; L2 flushed before each",
     }
+    out.update(extras)
     if world == 1 and args.cpu_budget > 0:
-        out["cpu_baseline"] = cpu_baseline(wl, args.cpu_budget)
+        cb, port = cpu_baseline(wl, args.cpu_budget)
+        out["cpu_baseline"] = cb
+        if port is not None:
+            out["cpu_baseline_port"] = port
     print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Extras printed beside the headline: parity of the multi-GPU exchanges against
+# the single-GPU transforms, and the four-step 2^30 at this GPU count against
+# the same algorithm on one GPU.
+# ---------------------------------------------------------------------------
+
+
+def _sum_sq(t):
+    return float((t.double() ** 2).sum())
+
+
+def multi_gpu_check(world, rank, dev):
+    """rel-L2 of fft_distributed (2^24; column-block input with transposed output, contiguous
+    input with natural output, and the NCCL exchange) and fft2_distributed (4096^2, both output
+    layouts) against trnfft.fft / trnfft.fft2 of the whole input on one GPU."""
+    import trnfft_b200 as trnfft
+    from trnfft_b200 import ComplexTensor
+    from trnfft_b200 import distributed as D
+
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(4242)  # same input on every rank
+    n = 1 << 24
+    xr = torch.randn(n, device=dev, generator=g)
+    xi = torch.randn(n, device=dev, generator=g)
+    X = trnfft.fft(ComplexTensor(xr.reshape(1, n), xi.reshape(1, n)))
+    Xr, Xi = X.real.reshape(-1), X.imag.reshape(-1)
+    N1, N2 = D._split_n(n)
+    r1 = N1 // world
+    c2 = N2 // world
+    # transposed output: Z[k1 local][k2] = X[k1 + N1 k2], k1 in this rank's block
+    want_t = (Xr.reshape(N2, N1)[:, rank * r1:(rank + 1) * r1].t(), Xi.reshape(N2, N1)[:, rank * r1:(rank + 1) * r1].t())
+    want_n = (Xr[rank * n // world:(rank + 1) * n // world], Xi[rank * n // world:(rank + 1) * n // world])
+    cases = {
+        "fft_distributed_2^24_columns_in_transposed": (
+            lambda: D.fft_distributed(ComplexTensor(*D.column_block(xr, xi, n, world, rank)), n,
+                                      natural_order=False, columns_in=True), want_t),
+        "fft_distributed_2^24_natural": (
+            lambda: D.fft_distributed(ComplexTensor(xr[rank * n // world:(rank + 1) * n // world],
+                                                    xi[rank * n // world:(rank + 1) * n // world]), n), want_n),
+        "fft_distributed_2^24_nccl_exchange": (
+            lambda: D.fft_distributed(ComplexTensor(xr[rank * n // world:(rank + 1) * n // world],
+                                                    xi[rank * n // world:(rank + 1) * n // world]), n,
+                                      exchange="nccl"), want_n),
+    }
+    s_ = 4096
+    fr = torch.randn(s_, s_, device=dev, generator=g)
+    fi = torch.randn(s_, s_, device=dev, generator=g)
+    F = trnfft.fft2(ComplexTensor(fr, fi))
+    h = s_ // world
+    rows = slice(rank * h, (rank + 1) * h)
+    cols = slice(rank * (s_ // world), (rank + 1) * (s_ // world))
+    cases["fft2_distributed_4096_natural"] = (
+        lambda: D.fft2_distributed(ComplexTensor(fr[rows], fi[rows])), (F.real[rows], F.imag[rows]))
+    cases["fft2_distributed_4096_column_blocks"] = (
+        lambda: D.fft2_distributed(ComplexTensor(fr[rows], fi[rows]), natural_order=False),
+        (F.real[:, cols], F.imag[:, cols]))
+    for name, (fn, (wr, wi)) in cases.items():
+        y = fn()
+        torch.cuda.synchronize()
+        num = _sum_sq(y.real.reshape(wr.shape) - wr) + _sum_sq(y.imag.reshape(wi.shape) - wi)
+        den = _sum_sq(wr) + _sum_sq(wi)
+        t = torch.tensor([num, den], dtype=torch.float64, device=dev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(t)
+        out[name] = float((t[0] / t[1]).sqrt())
+    D.clear_exchanges()
+    return out
+
+
+def large_extra(world, rank, dev, steps=10, warmup=3, logn=30):
+    """The four-step N=2^logn transform on `world` GPUs (max over ranks of the CUDA-event
+    time) and, on rank 0, the same algorithm on one GPU."""
+    from trnfft_b200 import ComplexTensor
+    from trnfft_b200 import distributed as D
+
+    n = 1 << logn
+    N1, N2 = D._split_n(n)
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    st = torch.cuda.current_stream(dev)
+
+    def time_fn(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        ts = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sum(ts) / len(ts)
+
+    res = {"n": f"2^{logn}", "split": f"{N1} x {N2}", "steps": steps}
+    if world > 1:
+        xr = torch.randn(N1, N2 // world, device=dev, generator=g)
+        xi = torch.randn(N1, N2 // world, device=dev, generator=g)
+        x = ComplexTensor(xr, xi)
+        ms = time_fn(lambda: D.fft_distributed(x, n, natural_order=False, columns_in=True))
+        res["ms"] = round(allreduce_max(ms, world), 4)
+        del x, xr, xi
+        D.clear_exchanges()
+        torch.cuda.empty_cache()
+    barrier(world)
+    if rank == 0:
+        xr = torch.randn(N1, N2, device=dev, generator=g)
+        xi = torch.randn(N1, N2, device=dev, generator=g)
+        x = ComplexTensor(xr, xi)
+        ms1 = time_fn(lambda: D.fft_four_step_local(x, n))
+        res["ms_1gpu"] = round(ms1, 4)
+        if world == 1:
+            res["ms"] = res["ms_1gpu"]
+        res["speedup_vs_1gpu"] = round(ms1 / res["ms"], 3)
+        res["gflops"] = round(c2c_flops(n, 1) / (res["ms"] / 1e3) / 1e9, 1)
+        del x, xr, xi
+        torch.cuda.empty_cache()
+    barrier(world)
+    return res
 
 
 def main():
@@ -782,6 +1082,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2c1024")
     ap.add_argument("--size", type=int, default=0, help="smaller case for profiling (large/fft2/linear)")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="skip the multi-GPU parity check and the four-step 2^30 line of the default run")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     try:

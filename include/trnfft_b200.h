@@ -97,9 +97,13 @@ TRNFFT_API int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* pa
  * trnfft.fft / trnfft.ifft (trnfft/api.py:22-35).
  * Power-of-two 4096 < n <= 16384 run as one row pass (one transform per
  * block); larger n (up to 2^30) as two to four column-tile passes
- * (four-step / six-step, trnfft/nki/multicore.py:151-219).  In-place calls
- * (in == out) are allowed; for n > 4096 they need `work`, a device buffer
- * of trnfft_plan_query's work_bytes; out-of-place calls need none (NULL). */
+ * (four-step / six-step, trnfft/nki/multicore.py:151-219).  Exactly
+ * in-place calls (out_re == in_re and out_im == in_im) are allowed and need
+ * no work area up to n = 16384; above that an in-place call needs `work`, a
+ * device buffer of trnfft_plan_query's work_bytes, disjoint from the data.
+ * Output planes that overlap the input in any other way are rejected
+ * (TRNFFT_INVALID_VALUE) up to n = 16384 and copied aside through `work`
+ * above it.  Out-of-place calls need no work area (NULL). */
 TRNFFT_API int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out_re,
                     float* out_im, int64_t batch, int inverse, void* work, void* stream);
 
@@ -120,7 +124,8 @@ TRNFFT_API int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, cons
  * allocator or memory pool, real-time callbacks that must not allocate,
  * runtimes that only lend fixed buffers).  No counterpart in the reference.
  *
- * Only power-of-two n > 4096 (the multi-pass sizes that need scratch) and
+ * Only power-of-two n > 4096 (the multi-pass plans; 8192 and 16384 run in
+ * place without touching the scratch, larger n copy their input into it) and
  * batch * n <= 2^21 complex values: the scratch is a fixed 16 MiB device
  * array that every GPU loading the library keeps until process exit.
  * Larger requests fail with TRNFFT_INVALID_VALUE.  The first call on a device
@@ -146,6 +151,33 @@ TRNFFT_API int trnfft_exec_c2c_inplace_noalloc(trnfft_plan_t plan, float* re, fl
 TRNFFT_API int trnfft_exec_stft(trnfft_plan_t plan, const float* signal, int64_t batch, int64_t length,
                                 int64_t hop, const float* window, int center, int pad_mode, int normalized,
                                 int onesided, int64_t frames, float* out_re, float* out_im, void* stream);
+
+/* Inverse short-time Fourier transform with windowed overlap-add, power-of-two
+ * n_fft = plan n (4..8192).  Replaces trnfft.istft (trnfft/api.py:368-470):
+ * each frame of the (batch, bins, frames) planes (bins = n_fft/2+1 when
+ * `onesided`, else n_fft, of which the real part of the inverse transform is
+ * used) is inverse-transformed, multiplied by `window` (n_fft floats, already
+ * zero-padded) and overlap-added every `hop` samples; samples whose envelope
+ * sum_f window[t - f*hop]^2 exceeds 1e-8 are divided by it, the others keep
+ * the unwindowed sum (api.py:450-452).  `normalized` undoes the forward
+ * 1/sqrt(n_fft).  `out` receives batch rows of out_len samples starting at
+ * overlap-add position n_fft/2 when `center` (else 0), zero past
+ * n_fft + (frames-1)*hop; the caller derives out_len from `length` as
+ * api.py:454-468 does.  One kernel, one pass over the spectrum. */
+TRNFFT_API int trnfft_exec_istft(trnfft_plan_t plan, const float* in_re, const float* in_im, int64_t batch,
+                                 int64_t frames, int64_t hop, const float* window, int center, int normalized,
+                                 int onesided, int64_t out_len, float* out, void* stream);
+
+/* Element-wise complex product out = mask * spec over `count` elements of
+ * planar float32 data, where element i uses mask element i % mask_count
+ * (mask_count divides count: a mask repeated over the leading axes).
+ * Replaces trnfft.nki.dispatch.complex_mask_apply (trnfft/nki/dispatch.py:
+ * 105-113) and its fused NKI kernel (dispatch.py:347-417).  The output may be
+ * the spectrogram's planes (in place); it may be the mask's planes only when
+ * mask_count == count.  On CUDA device `device`, enqueued on `stream`. */
+TRNFFT_API int trnfft_complex_mask_apply(const float* mask_re, const float* mask_im, int64_t mask_count,
+                                         const float* spec_re, const float* spec_im, float* out_re, float* out_im,
+                                         int64_t count, int device, void* stream);
 
 /* Work-area bytes trnfft_complex_linear needs: the TF32 hi/lo split of x and
  * W, 4*(M+N)*K floats.  -1 for negative sizes. */
@@ -197,7 +229,10 @@ TRNFFT_API int trnfft_ipc_close(int device, void* ptr);
  * replace the all-to-all of the reference's host-side transpose
  * (trnfft/nki/multicore.py:189-217).  The caller orders the ranks before
  * (peers done reading) and after (all stores landed) the call.  n > 1024
- * needs `work` of 2*n*inner floats. */
+ * needs `work` of 2*n*inner floats.  Every peer_re[q] / peer_im[q] must map
+ * at least rows_per_peer * peer_ld floats: the library cannot see the size of
+ * another process's allocation, and a smaller buffer receives stores past its
+ * end. */
 TRNFFT_API int trnfft_exec_fourstep_scatter(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re,
                                             const float* in_im, int64_t inner, int64_t ld_in, int inverse,
                                             int64_t col_offset, int npeers, float* const* peer_re,

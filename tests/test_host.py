@@ -100,3 +100,42 @@ def test_multicore_prime_raises_before_compute():
             multicore.multi_core_fft(trnfft.ComplexTensor(torch.randn(7), torch.zeros(7)))
     finally:
         multicore.set_multicore(False)
+
+
+def test_complex_layers_off_the_hot_path_match_their_definitions():
+    """ComplexConv1d, ComplexBatchNorm1d and ComplexModReLU (CPU, torch only) against the
+    complex arithmetic they define (trnfft/nn.py:52-129)."""
+    import torch
+
+    from trnfft_b200 import ComplexTensor
+    from trnfft_b200.nn import ComplexBatchNorm1d, ComplexConv1d, ComplexModReLU
+
+    torch.manual_seed(0)
+    conv = ComplexConv1d(3, 5, 4, stride=2, padding=1)
+    with torch.no_grad():
+        conv.bias_re.normal_()
+        conv.bias_im.normal_()
+    x = ComplexTensor(torch.randn(2, 3, 20), torch.randn(2, 3, 20))
+    y = conv(x)
+    xc = torch.complex(x.real, x.imag).to(torch.complex64)
+    kc = torch.complex(conv.conv_re.weight, conv.conv_im.weight)
+    bc = torch.complex(conv.bias_re, conv.bias_im)
+    want = torch.nn.functional.conv1d(xc, kc, bc, stride=2, padding=1)
+    assert torch.allclose(torch.complex(y.real, y.imag), want, atol=1e-5)
+
+    relu = ComplexModReLU(7)
+    with torch.no_grad():
+        relu.bias.normal_()
+    z = ComplexTensor(torch.randn(4, 5, 7), torch.randn(4, 5, 7))
+    out = relu(z)
+    zc = torch.complex(z.real, z.imag)
+    r = zc.abs()
+    want = torch.relu(r + relu.bias) * zc / r.clamp_min(1e-8)
+    assert torch.allclose(torch.complex(out.real, out.imag), want, atol=1e-6)
+
+    bn = ComplexBatchNorm1d(3)
+    u = ComplexTensor(torch.randn(8, 3, 10), torch.randn(8, 3, 10))
+    v = bn(u)
+    ref = torch.nn.BatchNorm1d(3)
+    assert torch.allclose(v.real, ref(u.real), atol=1e-6)
+    assert torch.allclose(v.imag, torch.nn.BatchNorm1d(3)(u.imag), atol=1e-6)

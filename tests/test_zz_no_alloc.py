@@ -30,7 +30,7 @@ def _reference(plan, xr, xi, inverse):
     return yr, yi
 
 
-@pytest.mark.parametrize("n,batch", [(1 << 13, 4), (1 << 21, 1)])
+@pytest.mark.parametrize("n,batch", [(1 << 13, 4), (1 << 21, 1), (1 << 13, 256), (1 << 20, 2)])
 def test_noalloc_matches_exec_c2c_twice(n, batch):
     dev = torch.device("cuda", torch.cuda.current_device())
     plan = _lib.device_plan(n, dev)
@@ -55,6 +55,12 @@ def test_noalloc_rejects_sizes_beyond_scratch():
     x = torch.zeros(2, n, device=dev)
     with pytest.raises(ValueError, match="exceeds the fixed scratch"):
         _lib.call("trnfft_exec_c2c_inplace_noalloc", plan.handle, _lib.ptr(x), _lib.ptr(x), 2, 0,
+                  _lib.stream_ptr(dev))
+    # 2^20 x 3 is one transform more than the scratch holds (2^20 x 2 fits exactly)
+    mid = _lib.device_plan(1 << 20, dev)
+    y = torch.zeros(3, 1 << 20, device=dev)
+    with pytest.raises(ValueError, match="exceeds the fixed scratch"):
+        _lib.call("trnfft_exec_c2c_inplace_noalloc", mid.handle, _lib.ptr(y), _lib.ptr(y), 3, 0,
                   _lib.stream_ptr(dev))
     small = _lib.device_plan(1024, dev)
     with pytest.raises(ValueError, match="only power-of-two n > 4096"):

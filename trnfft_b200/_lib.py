@@ -56,6 +56,8 @@ SIGNATURES = {
     "trnfft_exec_fourstep_scatter": (_INT, [_P, _P, _P, _P, _I64, _I64, _INT, _I64, _INT,
                                             ctypes.POINTER(_P), ctypes.POINTER(_P), _I64, _I64, _I64, _P, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
+    "trnfft_exec_istft": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _INT, _INT, _INT, _I64, _P, _P]),
+    "trnfft_complex_mask_apply": (_INT, [_P, _P, _I64, _P, _P, _P, _P, _I64, _INT, _P]),
     "trnfft_exec_c2r": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
 }
 

@@ -139,6 +139,18 @@ def _r2c_native(n: int) -> bool:
     return n >= 4 and (n & (n - 1)) == 0 and n <= 8192
 
 
+def _real_kernel(n: int, device: torch.device) -> bool:
+    """Whether trnfft_exec_r2c / _c2r have a direct kernel for n on this device:
+    powers of two 4..8192 (packed real rows) and Bluestein lengths whose padded
+    size m fits one block (m <= 16384, the fused kernel's real-input modes)."""
+    if _r2c_native(n):
+        return True
+    if n < 3 or (n & (n - 1)) == 0:
+        return False
+    plan = _lib.device_plan(n, device)
+    return plan.algorithm == _lib.ALG_BLUESTEIN and plan.padded_n <= 16384
+
+
 def r2c_raw(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """rfft along the last axis: (..., n) real -> (..., n//2+1) complex."""
     _check(x, "input")
@@ -147,10 +159,10 @@ def r2c_raw(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     lead = x.shape[:-1]
     a = _flat(x, n)
     batch = a.shape[0]
-    if not _r2c_native(n):
+    if not _real_kernel(n, a.device):
         yr, yi = c2c_raw(a, torch.zeros_like(a), False)
         return yr[:, :h].reshape(*lead, h), yi[:, :h].reshape(*lead, h)
-    if a.data_ptr() % 8:
+    if _r2c_native(n) and a.data_ptr() % 8:
         a = a.clone()
     yr = torch.empty(batch, h, dtype=torch.float32, device=a.device)
     yi = torch.empty(batch, h, dtype=torch.float32, device=a.device)
@@ -188,7 +200,7 @@ def c2r_raw(xr: torch.Tensor, xi: torch.Tensor, n: int) -> torch.Tensor:
     _check(xi, "imaginary part")
     h = xr.shape[-1]
     lead = xr.shape[:-1]
-    if _r2c_native(n) and h == n // 2 + 1:
+    if h == n // 2 + 1 and _real_kernel(n, xr.device):
         a = _flat(xr, h)
         b = _flat(xi, h)
         batch = a.shape[0]
@@ -288,7 +300,7 @@ def c2c(xr, xi, inverse: bool):
 def r2c(x):
     if _needs_grad(x):
         n = x.shape[-1]
-        if _r2c_native(n):
+        if x.is_cuda and _real_kernel(n, x.device):
             return _R2C.apply(x)
         h = n // 2 + 1
         yr, yi = _C2C.apply(x, torch.zeros_like(x), False)
@@ -298,7 +310,7 @@ def r2c(x):
 
 def c2r(xr, xi, n: int):
     if _needs_grad(xr, xi):
-        if _r2c_native(n) and xr.shape[-1] == n // 2 + 1:
+        if xr.is_cuda and xr.shape[-1] == n // 2 + 1 and _real_kernel(n, xr.device):
             return _C2R.apply(xr, xi, n)
         fr, fi = hermitian_extend(xr, xi, n)
         yr, _ = _C2C.apply(fr, fi, True)
@@ -371,9 +383,49 @@ def stft(x: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool, p
     return yr.reshape(*lead, nb, nf), yi.reshape(*lead, nb, nf)
 
 
+def istft_out_len(n_fft: int, frames: int, hop: int, center: bool, length) -> int:
+    """Samples istft returns (trnfft/api.py:454-468): overlap-add length, minus the centre
+    padding (the tail padding only when `length` is None), or `length` itself."""
+    exp_len = n_fft + (frames - 1) * hop
+    cur = exp_len
+    if center:
+        p = n_fft // 2
+        cur = exp_len - p
+        if cur > p and length is None:
+            cur -= p
+    return cur if length is None else int(length)
+
+
 def istft(sr: torch.Tensor, si: torch.Tensor, n_fft: int, hop: int, w: torch.Tensor, center: bool,
           normalized: bool, onesided: bool, length):
-    """Inverse transform per frame and windowed overlap-add (trnfft/api.py:368-470)."""
+    """Inverse transform per frame and windowed overlap-add (trnfft/api.py:368-470).
+
+    Power-of-two n_fft up to 8192 without autograd runs the fused kernel
+    (trnfft_exec_istft); other cases compose the library's inverse transforms with a
+    device overlap-add."""
+    fused = (4 <= n_fft <= 8192 and (n_fft & (n_fft - 1)) == 0 and not _needs_grad(sr, si, w)
+             and sr.shape[-2] == (n_fft // 2 + 1 if onesided else n_fft))
+    if not fused:
+        return _istft_composite(sr, si, n_fft, hop, w, center, normalized, onesided, length)
+    _check(sr, "real part")
+    _check(si, "imaginary part")
+    lead = sr.shape[:-2]
+    fb, nf = sr.shape[-2], sr.shape[-1]
+    a = sr.reshape(-1, fb, nf).contiguous()
+    b = si.reshape(-1, fb, nf).contiguous()
+    B = a.shape[0]
+    out_len = istft_out_len(n_fft, nf, hop, center, length)
+    y = torch.empty(B, out_len, dtype=torch.float32, device=a.device)
+    if B and out_len:
+        plan = _lib.device_plan(n_fft, a.device)
+        _lib.call("trnfft_exec_istft", plan.handle, _lib.ptr(a), _lib.ptr(b), B, nf, hop,
+                  _lib.ptr(w.contiguous()), int(bool(center)), int(bool(normalized)), int(bool(onesided)),
+                  out_len, _lib.ptr(y), _lib.stream_ptr(a.device))
+    return y.reshape(*lead, out_len)
+
+
+def _istft_composite(sr, si, n_fft, hop, w, center, normalized, onesided, length):
+    """istft from the library's inverse transforms plus a torch overlap-add (autograd, other n_fft)."""
     if normalized:
         sc = n_fft ** 0.5
         sr = sr * sc

@@ -530,13 +530,31 @@ int trnfft_plan_query(trnfft_plan_t plan, int* algorithm, int64_t* padded_n, int
   // a multi-pass Bluestein transform (m > 16384) always needs two m-point buffers.
   if (work_bytes) {
     if (plan->algorithm == TRNFFT_ALG_MULTIPASS)
-      *work_bytes = (int64_t)(2 * sizeof(float)) * plan->n * batch;
+      *work_bytes = (int64_t)(2 * sizeof(float)) * plan->n * batch;  // needed only above 16384 points
     else if (plan->algorithm == TRNFFT_ALG_BLUESTEIN && plan->sub)
       *work_bytes = (int64_t)(4 * sizeof(float)) * plan->m * batch;
     else
       *work_bytes = 0;
   }
   return TRNFFT_SUCCESS;
+}
+
+// [a, a + abytes) and [b, b + bbytes) share a byte
+static bool ranges_overlap(const void* a, size_t abytes, const void* b, size_t bbytes) {
+  const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+  return x < y + bbytes && y < x + abytes;
+}
+
+// How the output planes of a transform over `count` floats per plane relate
+// to its input planes: 0 disjoint, 1 exactly in place (out_re == in_re and
+// out_im == in_im), 2 any other overlap.
+static int alias_kind(const float* in_re, const float* in_im, const float* out_re, const float* out_im,
+                      size_t count) {
+  const size_t b = count * sizeof(float);
+  const bool any = ranges_overlap(in_re, b, out_re, b) || ranges_overlap(in_re, b, out_im, b) ||
+                   ranges_overlap(in_im, b, out_re, b) || ranges_overlap(in_im, b, out_im, b);
+  if (!any) return 0;
+  return (in_re == out_re && in_im == out_im) ? 1 : 2;
 }
 
 static int check_ptrs(const char* fn, std::initializer_list<const void*> ps, size_t align) {
@@ -560,6 +578,11 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t n = plan->n;
   cudaError_t e = cudaSuccess;
+  // One-pass kernels read each row whole before writing it: exactly in place
+  // is fine, any other overlap of input and output planes is not.
+  if (plan->algorithm != TRNFFT_ALG_MULTIPASS &&
+      alias_kind(in_re, in_im, out_re, out_im, (size_t)n * (size_t)batch) == 2)
+    return fail(TRNFFT_INVALID_VALUE, "exec_c2c: input and output planes overlap without being the same planes");
   switch (plan->algorithm) {
     case TRNFFT_ALG_COPY: {
       const size_t bytes = sizeof(float) * (size_t)batch;
@@ -588,16 +611,28 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
         return fail(TRNFFT_UNSUPPORTED, "exec_c2c: n=2^%d above the supported 2^%d", plan->logn, kMaxMultipassLog);
       const float* xr = in_re;
       const float* xi = in_im;
-      if (in_re == out_re || in_im == out_im) {
-        // the first pass scatters rows, so an in-place call copies the input aside
-        if (!work) return fail(TRNFFT_INVALID_VALUE, "exec_c2c: in-place n=%lld needs the work area", (long long)n);
+      // Rows of up to 16384 points are one pass in which every block reads a
+      // whole row before writing it, so an exactly in-place call needs no copy.
+      // More passes scatter rows across the whole transform: then any overlap
+      // of input and output (in place, or planes that partly overlap) first
+      // copies the input into the work area.
+      const int ak = alias_kind(in_re, in_im, out_re, out_im, (size_t)n * (size_t)batch);
+      if (ak == 2 || (ak == 1 && plan->logn > kMaxRowBlockLog)) {
+        if (!work)
+          return fail(TRNFFT_INVALID_VALUE, "exec_c2c: n=%lld with overlapping input and output needs the work area",
+                      (long long)n);
         float* w = static_cast<float*>(work);
-        const size_t bytes = sizeof(float) * (size_t)n * (size_t)batch;
-        e = cudaMemcpyAsync(w, in_re, bytes, cudaMemcpyDeviceToDevice, st);
-        if (e == cudaSuccess) e = cudaMemcpyAsync(w + (size_t)n * batch, in_im, bytes, cudaMemcpyDeviceToDevice, st);
+        const size_t cnt = (size_t)n * (size_t)batch;
+        if (ranges_overlap(w, 2 * cnt * sizeof(float), in_re, cnt * sizeof(float)) ||
+            ranges_overlap(w, 2 * cnt * sizeof(float), in_im, cnt * sizeof(float)) ||
+            ranges_overlap(w, 2 * cnt * sizeof(float), out_re, cnt * sizeof(float)) ||
+            ranges_overlap(w, 2 * cnt * sizeof(float), out_im, cnt * sizeof(float)))
+          return fail(TRNFFT_INVALID_VALUE, "exec_c2c: the work area overlaps the data");
+        e = cudaMemcpyAsync(w, in_re, cnt * sizeof(float), cudaMemcpyDeviceToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(w + cnt, in_im, cnt * sizeof(float), cudaMemcpyDeviceToDevice, st);
         if (e != cudaSuccess) break;
         xr = w;
-        xi = w + (size_t)n * batch;
+        xi = w + cnt;
       }
       e = run_rows_multipass(plan, xr, xi, out_re, out_im, batch, inverse != 0, st);
       break;
@@ -919,6 +954,71 @@ int trnfft_exec_c2r(trnfft_plan_t plan, const float* in_re, const float* in_im, 
     return fail(TRNFFT_UNSUPPORTED, "exec_c2r: n=%lld not supported yet", (long long)n);
   }
   if (e != cudaSuccess) return cuda_fail(e, "exec_c2r");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_exec_istft(trnfft_plan_t plan, const float* in_re, const float* in_im, int64_t batch, int64_t frames,
+                      int64_t hop, const float* window, int center, int normalized, int onesided, int64_t out_len,
+                      float* out, void* stream) {
+  if (!plan) return fail(TRNFFT_INVALID_VALUE, "exec_istft: null plan");
+  const int64_t n = plan->n;
+  if (plan->logn < 2 || plan->logn > 13)
+    return fail(TRNFFT_UNSUPPORTED, "exec_istft: n_fft=%lld (power of two 4..8192 only)", (long long)n);
+  if (batch < 0 || frames < 1 || hop < 1 || out_len < 0)
+    return fail(TRNFFT_INVALID_VALUE, "exec_istft: bad batch/frames/hop/out_len");
+  if (batch == 0 || out_len == 0) return TRNFFT_SUCCESS;
+  int rc = check_ptrs("exec_istft", {in_re, in_im, window, out}, 4);
+  if (rc) return rc;
+  const int64_t nbins = onesided ? n / 2 + 1 : n;
+  const size_t in_bytes = sizeof(float) * (size_t)batch * (size_t)nbins * (size_t)frames;
+  const size_t out_bytes = sizeof(float) * (size_t)batch * (size_t)out_len;
+  if (ranges_overlap(out, out_bytes, in_re, in_bytes) || ranges_overlap(out, out_bytes, in_im, in_bytes))
+    return fail(TRNFFT_INVALID_VALUE, "exec_istft: the output overlaps the input spectrum");
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_istft: cannot select device %d", plan->device);
+  IstftArgs a;
+  std::memset(&a, 0, sizeof a);
+  a.xr = in_re;
+  a.xi = in_im;
+  a.window = window;
+  a.y = out;
+  a.batch = batch;
+  a.frames = frames;
+  a.hop = hop;
+  a.out_len = out_len;
+  a.pad_front = center ? n / 2 : 0;
+  a.exp_len = n + (frames - 1) * hop;
+  a.total = a.exp_len > a.pad_front + out_len ? a.exp_len : a.pad_front + out_len;
+  a.onesided = onesided ? 1 : 0;
+  a.scale = (float)((normalized ? std::sqrt((double)n) : 1.0) / (double)n);
+  cudaError_t e = launch_istft(plan->logn, a, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "exec_istft");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_complex_mask_apply(const float* mask_re, const float* mask_im, int64_t mask_count, const float* spec_re,
+                              const float* spec_im, float* out_re, float* out_im, int64_t count, int device,
+                              void* stream) {
+  if (count < 0 || mask_count < 0) return fail(TRNFFT_INVALID_VALUE, "complex_mask_apply: negative size");
+  if (count == 0) return TRNFFT_SUCCESS;
+  if (mask_count == 0 || count % mask_count)
+    return fail(TRNFFT_INVALID_VALUE, "complex_mask_apply: count %lld is not a multiple of mask_count %lld",
+                (long long)count, (long long)mask_count);
+  int rc = check_ptrs("complex_mask_apply", {mask_re, mask_im, spec_re, spec_im, out_re, out_im}, 4);
+  if (rc) return rc;
+  const size_t mb = sizeof(float) * (size_t)mask_count, cb = sizeof(float) * (size_t)count;
+  for (const float* o : {out_re, out_im}) {
+    const bool mask_ok = !(ranges_overlap(o, cb, mask_re, mb) || ranges_overlap(o, cb, mask_im, mb)) ||
+                         (mask_count == count && (o == mask_re || o == mask_im));
+    if (!mask_ok) return fail(TRNFFT_INVALID_VALUE, "complex_mask_apply: output overlaps a repeated mask");
+  }
+  if (ranges_overlap(out_re, cb, out_im, cb))
+    return fail(TRNFFT_INVALID_VALUE, "complex_mask_apply: output planes overlap");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "complex_mask_apply: cannot select device %d", device);
+  cudaError_t e = launch_cmul(mask_re, mask_im, mask_count, spec_re, spec_im, out_re, out_im, count,
+                              reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "complex_mask_apply");
   return TRNFFT_SUCCESS;
 }
 

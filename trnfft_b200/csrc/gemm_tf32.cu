@@ -28,6 +28,7 @@
 //              lanes x 128 columns), float32 accumulation, bias add, store.
 // Every wait is bounded: on timeout the CTA records the device status word,
 // drains what it issued (bounded), frees its TMEM and exits.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -359,6 +360,8 @@ static bool make_map(CUtensorMap* m, const float* ptr, long long rows, long long
   return r == CUDA_SUCCESS;
 }
 
+static constexpr int kGemmMaxDevices = 64;
+
 cudaError_t launch_gemm_tf32(const GemmArgs& g, cudaStream_t st) {
   using namespace gemm;
   if (g.M <= 0 || g.N <= 0 || g.K <= 0) return cudaSuccess;
@@ -379,11 +382,17 @@ cudaError_t launch_gemm_tf32(const GemmArgs& g, cudaStream_t st) {
     segs.b_idx[s] = g.seg_b[s];
     segs.neg[s] = g.seg_neg[s];
   }
-  static bool attr_done = false;
-  if (!attr_done) {
+  // The dynamic shared-memory opt-in is a per-device function attribute: set
+  // it once per device (the current one), under a flag per device that
+  // concurrent first calls may both pass (setting it twice is harmless).
+  static std::atomic<bool> attr_done[kGemmMaxDevices];
+  int dev = 0;
+  cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return de;
+  if (dev < 0 || dev >= kGemmMaxDevices || !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tf32, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    if (dev >= 0 && dev < kGemmMaxDevices) attr_done[dev].store(true, std::memory_order_release);
   }
   dim3 grid((unsigned)((g.N + BN - 1) / BN), (unsigned)((g.M + BM - 1) / BM));
   k_gemm_tf32<<<grid, THREADS, SMEM, st>>>(am[0], am[1], am[2], am[3], bm[0], bm[1], bm[2], bm[3], segs, g.C,

@@ -100,6 +100,29 @@ struct StftArgs {
 
 cudaError_t launch_stft(int logn, const StftArgs& a, cudaStream_t st);
 
+// Fused inverse STFT (istft.cu): input planes (batch, bins, frames) with bins =
+// n/2+1 (onesided) or n; output (batch, out_len): sample o is overlap-add
+// position t = o + pad_front (zero where t >= exp_len = n + (frames-1)*hop).
+// scale multiplies every inverse-transformed sample (1/n, times sqrt(n) when
+// the forward transform was normalised).  seg / nseg are set by the launcher.
+struct IstftArgs {
+  const float* xr;
+  const float* xi;
+  const float* window;  // n entries
+  float* y;
+  long long batch, frames, hop, out_len, pad_front, exp_len, total;
+  int onesided;
+  float scale;
+  int seg;
+  long long nseg;
+};
+
+cudaError_t launch_istft(int logn, const IstftArgs& a, cudaStream_t st);
+
+// Element-wise complex product y = m[i mod mcount] * s[i] (mask.cu), i < count.
+cudaError_t launch_cmul(const float* mr, const float* mi, long long mcount, const float* sr, const float* si,
+                        float* yr, float* yi, long long count, cudaStream_t st);
+
 // TF32 tensor-core GEMM with signed K-segments (gemm_tf32.cu):
 // C = sum_s (seg_neg[s] ? -1 : 1) * A[seg_a[s]] * B[seg_b[s]]^T (+ bias),
 // A_i: M x K (lda), B_i: N x K (ldb), C: M x N (ldc), row-major float32.

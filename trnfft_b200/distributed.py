@@ -151,7 +151,7 @@ def _cuda_col_fft_tw(re, im, inverse, n, col0):
     plan = _lib.device_plan(n1, re.device)
     twp = _lib.device_plan(n, re.device)
     _lib.call("trnfft_exec_c2c_axis_tw", plan.handle, twp.handle, _lib.ptr(re), _lib.ptr(im), _lib.ptr(yr),
-              _lib.ptr(yi), 1, cols, int(bool(inverse)), col0, _lib.stream_ptr(re.device))
+              _lib.ptr(yi), 1, cols, 0, 0, int(bool(inverse)), col0, _lib.stream_ptr(re.device))
     return yr, yi
 
 
@@ -258,7 +258,18 @@ class _PeerExchange:
             pass
 
 
+# Peer-exchange row buffers per (n, world size, device, process group).  Each
+# entry keeps a reference to its group, so the group's id() in the key cannot
+# be reused by a new group while the entry exists.  The buffers (2 x n/P
+# floats per rank) and their IPC mappings stay allocated until
+# clear_exchanges() or process exit.
 _exchanges: dict = {}
+
+
+def clear_exchanges() -> None:
+    """Release every cached peer-exchange buffer and IPC mapping (call on all ranks,
+    with no transform in flight, e.g. before destroying a process group)."""
+    _exchanges.clear()
 
 
 def _device_barrier(group, dev):
@@ -285,9 +296,10 @@ def _four_step_peer(ar, ai, n, group, inverse, natural_order, chunks=1):
     r1, c2 = N1 // P, N2 // P
     dev = ar.device
     key = (n, P, dev.index, id(group))
-    ex = _exchanges.get(key)
-    if ex is None:
-        ex = _exchanges[key] = _PeerExchange(n, group, dev)
+    entry = _exchanges.get(key)
+    if entry is None or entry[0] is not group:
+        entry = _exchanges[key] = (group, _PeerExchange(n, group, dev))
+    ex = entry[1]
     plan = _lib.device_plan(N1, dev)
     twp = _lib.device_plan(n, dev)
     nch = chunks if (chunks > 1 and c2 % chunks == 0 and c2 // chunks >= 32) else 1
@@ -331,6 +343,22 @@ def _cuda_row_fft(re, im, inverse):
     from . import _ops
 
     return _ops.c2c_raw(re, im, inverse)
+
+
+def fft_four_step_local(x_cols: ComplexTensor, n: int, inverse: bool = False) -> ComplexTensor:
+    """One-GPU run of the same four-step split that ``fft_distributed`` uses (for P = 1).
+
+    Input: the [N1][N2] column view of x (``column_block(x, n, 1, 0)``, which is x itself
+    reshaped); output Z[k1][k2] = X[k1 + N1*k2] (the transposed order).  Three HBM passes:
+    two column passes with the twiddle fused into the second, one row pass.  This is the
+    single-GPU baseline the distributed transform's speed-up is measured against.
+    """
+    N1, N2 = _split_n(n)
+    xr = x_cols.real.reshape(N1, N2).float().contiguous()
+    xi = x_cols.imag.reshape(N1, N2).float().contiguous()
+    yr, yi = _cuda_col_fft_tw(xr, xi, inverse, n, 0)
+    zr, zi = _cuda_row_fft(yr, yi, inverse)
+    return ComplexTensor(zr, zi)
 
 
 def column_block(x_full_re: torch.Tensor, x_full_im: torch.Tensor, n: int, world: int, rank: int):

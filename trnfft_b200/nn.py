@@ -2,9 +2,9 @@
 
 ``ComplexLinear`` is on the hot path: its forward runs the library's complex
 GEMM (``trnfft_b200.nki.dispatch.complex_linear``).  ``ComplexConv1d``,
-``ComplexBatchNorm1d`` and ``ComplexModReLU`` are kept for API compatibility;
-they are compositions of torch layers exactly as in the reference
-(trnfft/nn.py:52-129).
+``ComplexBatchNorm1d`` and ``ComplexModReLU`` are kept for API compatibility
+(same parameters and values as trnfft/nn.py:52-129); they are off the FFT hot
+path and written as plain torch compositions.
 """
 
 from __future__ import annotations
@@ -44,31 +44,41 @@ class ComplexLinear(nn.Module):
 
 
 class ComplexConv1d(nn.Module):
-    """Complex-valued 1-D convolution (trnfft/nn.py:52-86)."""
+    """Complex 1-D convolution with the reference's parameters (trnfft/nn.py:52-86).
+
+    Parameters: ``conv_re`` / ``conv_im`` (``nn.Conv1d`` without bias, the
+    real and imaginary kernel) and optional ``bias_re`` / ``bias_im``.  The
+    forward pass runs ONE real convolution over the stacked channels
+    [x_re; x_im] with the 2x2 block kernel [[K_re, -K_im], [K_im, K_re]], whose
+    output channels are then [y_re; y_im] = [K_re*x_re - K_im*x_im;
+    K_im*x_re + K_re*x_im].  Not on the FFT hot path.
+    """
 
     def __init__(self, in_channels: int, out_channels: int, kernel_size: int, stride: int = 1,
                  padding: int = 0, bias: bool = True):
         super().__init__()
         self.conv_re = nn.Conv1d(in_channels, out_channels, kernel_size, stride=stride, padding=padding, bias=False)
         self.conv_im = nn.Conv1d(in_channels, out_channels, kernel_size, stride=stride, padding=padding, bias=False)
-        if bias:
-            self.bias_re = nn.Parameter(torch.zeros(out_channels))
-            self.bias_im = nn.Parameter(torch.zeros(out_channels))
-        else:
-            self.bias_re = None
-            self.bias_im = None
+        self.bias_re = nn.Parameter(torch.zeros(out_channels)) if bias else None
+        self.bias_im = nn.Parameter(torch.zeros(out_channels)) if bias else None
 
     def forward(self, x: ComplexTensor) -> ComplexTensor:
-        re = self.conv_re(x.real) - self.conv_im(x.imag)
-        im = self.conv_re(x.imag) + self.conv_im(x.real)
+        kr, ki = self.conv_re.weight, self.conv_im.weight
+        block = torch.cat([torch.cat([kr, -ki], dim=1), torch.cat([ki, kr], dim=1)], dim=0)
+        b = None
         if self.bias_re is not None:
-            re = re + self.bias_re.unsqueeze(-1)
-            im = im + self.bias_im.unsqueeze(-1)
-        return ComplexTensor(re, im)
+            b = torch.cat([self.bias_re, self.bias_im])
+        y = torch.nn.functional.conv1d(torch.cat([x.real, x.imag], dim=-2), block, b,
+                                       stride=self.conv_re.stride, padding=self.conv_re.padding)
+        c = kr.shape[0]
+        return ComplexTensor(y[..., :c, :], y[..., c:, :])
 
 
 class ComplexBatchNorm1d(nn.Module):
-    """Independent batch norm of the real and imaginary parts (trnfft/nn.py:89-104)."""
+    """Batch normalisation of the real and the imaginary plane as separate channels
+    (trnfft/nn.py:89-104: two independent ``BatchNorm1d``; no whitening of the
+    complex covariance).  Keeps the reference's ``bn_re`` / ``bn_im`` modules
+    (and state-dict keys); the statistics of each plane are its own."""
 
     def __init__(self, num_features: int, eps: float = 1e-5):
         super().__init__()
@@ -76,23 +86,21 @@ class ComplexBatchNorm1d(nn.Module):
         self.bn_im = nn.BatchNorm1d(num_features, eps=eps)
 
     def forward(self, x: ComplexTensor) -> ComplexTensor:
-        return ComplexTensor(self.bn_re(x.real), self.bn_im(x.imag))
+        planes = [bn(p) for bn, p in ((self.bn_re, x.real), (self.bn_im, x.imag))]
+        return ComplexTensor(*planes)
 
 
 class ComplexModReLU(nn.Module):
-    """f(z) = ReLU(|z| + b) z / |z| (trnfft/nn.py:107-129)."""
+    """modReLU: keeps the phase of z and maps the modulus r = |z| to max(r + b, 0)
+    (trnfft/nn.py:107-129), with one learnt offset b per feature, broadcast
+    along the LAST axis as the reference does.  The gain
+    max(r + b, 0) / max(r, 1e-8) multiplies both planes."""
 
     def __init__(self, num_features: int):
         super().__init__()
         self.bias = nn.Parameter(torch.zeros(num_features))
 
     def forward(self, x: ComplexTensor) -> ComplexTensor:
-        mag = x.abs()
-        bias = self.bias
-        while bias.dim() < mag.dim():
-            bias = bias.unsqueeze(0)
-        if mag.dim() > bias.dim():
-            bias = bias.unsqueeze(-1)
-        activated = torch.relu(mag + bias)
-        scale = activated / torch.clamp(mag, min=1e-8)
-        return ComplexTensor(x.real * scale, x.imag * scale)
+        r = x.abs()
+        gain = torch.relu(r + self.bias) / r.clamp_min(1e-8)
+        return ComplexTensor(x.real * gain, x.imag * gain)
