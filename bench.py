@@ -24,6 +24,7 @@ cores, on a bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -159,7 +160,9 @@ def dist_setup():
 
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            # a short collective timeout: a rank that stops answering ends the run in minutes
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                    timeout=datetime.timedelta(seconds=240))
         else:
             dist.init_process_group("gloo")
     return world, rank, local
@@ -1031,11 +1034,12 @@ def large_extra(world, rank, dev, steps=10, warmup=3, logn=30):
     g = torch.Generator(device=dev).manual_seed(99 + rank)
     st = torch.cuda.current_stream(dev)
 
-    def time_fn(fn):
+    def time_fn(fn, collective):
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
-        barrier(world)
+        if collective:
+            barrier(world)
         ts = []
         for _ in range(steps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1051,7 +1055,7 @@ def large_extra(world, rank, dev, steps=10, warmup=3, logn=30):
         xr = torch.randn(N1, N2 // world, device=dev, generator=g)
         xi = torch.randn(N1, N2 // world, device=dev, generator=g)
         x = ComplexTensor(xr, xi)
-        ms = time_fn(lambda: D.fft_distributed(x, n, natural_order=False, columns_in=True))
+        ms = time_fn(lambda: D.fft_distributed(x, n, natural_order=False, columns_in=True), True)
         res["ms"] = round(allreduce_max(ms, world), 4)
         del x, xr, xi
         D.clear_exchanges()
@@ -1061,7 +1065,7 @@ def large_extra(world, rank, dev, steps=10, warmup=3, logn=30):
         xr = torch.randn(N1, N2, device=dev, generator=g)
         xi = torch.randn(N1, N2, device=dev, generator=g)
         x = ComplexTensor(xr, xi)
-        ms1 = time_fn(lambda: D.fft_four_step_local(x, n))
+        ms1 = time_fn(lambda: D.fft_four_step_local(x, n), False)  # rank 0 alone: no collective
         res["ms_1gpu"] = round(ms1, 4)
         if world == 1:
             res["ms"] = res["ms_1gpu"]

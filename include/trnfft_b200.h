@@ -138,6 +138,30 @@ TRNFFT_API int trnfft_exec_c2c_axis(trnfft_plan_t plan, const float* in_re, cons
 TRNFFT_API int trnfft_exec_c2c_inplace_noalloc(trnfft_plan_t plan, float* re, float* im, int64_t batch,
                                                int inverse, void* stream);
 
+/* Double precision.  trnfft_plan_enable_f64 builds the plan's fp64 tables
+ * (power of two n up to 2^24; any other n whose Bluestein length m is at most
+ * 2^24); it allocates device memory and synchronises, so call it before any
+ * stream capture.  trnfft_plan_query_f64 gives the work-area bytes
+ * trnfft_exec_c2c_f64 needs for `batch` transforms (0 for powers of two up to
+ * 4096).  trnfft_exec_c2c_f64 is trnfft_exec_c2c on planar float64 data with
+ * every stage (twiddles, chirp, filter spectrum, butterflies) in fp64.
+ * Replaces the reference's accuracy mode precision="double": the fp64
+ * Bluestein pipeline (trnfft/fft_core.py:1306-1309, 1372-1374) and the fp64
+ * DFT-GEMM for power-of-two n (_fft_via_gemm_double, fft_core.py:254-298,
+ * selected at :1108-1110), and its torch backend on float64 tensors.
+ * In-place calls are allowed; partly overlapping planes are rejected. */
+TRNFFT_API int trnfft_plan_enable_f64(trnfft_plan_t plan);
+TRNFFT_API int trnfft_plan_query_f64(trnfft_plan_t plan, int64_t batch, int64_t* work_bytes);
+TRNFFT_API int trnfft_exec_c2c_f64(trnfft_plan_t plan, const double* in_re, const double* in_im, double* out_re,
+                                   double* out_im, int64_t batch, int inverse, void* work, void* stream);
+
+/* Convert `count` values between float32 and float64 on `device` (to_double
+ * != 0: float -> double).  Used to run float32 data through the fp64
+ * transforms of precision="double" (the reference casts with .double() and
+ * back, fft_core.py:1308-1309, 1372-1374). */
+TRNFFT_API int trnfft_convert_f32_f64(const void* src, void* dst, int64_t count, int to_double, int device,
+                                      void* stream);
+
 /* Short-time Fourier transform of `batch` real signals of `length` samples,
  * power-of-two n_fft = plan n (4..8192).  Replaces trnfft.stft
  * (trnfft/api.py:291-365): frames start every `hop` samples of the signal

@@ -15,8 +15,9 @@ import torch
 from . import _lib
 
 
-def place(*ts: torch.Tensor):
-    """Return ([float32 CUDA tensors], restore) for the given tensors."""
+def place(*ts: torch.Tensor, allow_f64: bool = False):
+    """Return ([CUDA tensors], restore) for the given tensors: float32, or float64 when
+    ``allow_f64`` and the first tensor is float64 (the transforms that have fp64 kernels)."""
     dev = None
     for t in ts:
         if t is not None and t.is_cuda:
@@ -27,12 +28,13 @@ def place(*ts: torch.Tensor):
         _lib.require_cuda()
         dev = torch.device("cuda", torch.cuda.current_device())
     odt = ts[0].dtype
-    out = [None if t is None else t.to(device=dev, dtype=torch.float32) for t in ts]
+    work_dt = torch.float64 if (allow_f64 and odt == torch.float64) else torch.float32
+    out = [None if t is None else t.to(device=dev, dtype=work_dt) for t in ts]
 
     def restore(t: torch.Tensor) -> torch.Tensor:
         if host:
             t = t.to("cpu")
-        if odt.is_floating_point and odt != torch.float32:
+        if odt.is_floating_point and odt != t.dtype:
             t = t.to(odt)
         return t
 

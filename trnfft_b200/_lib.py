@@ -56,6 +56,10 @@ SIGNATURES = {
     "trnfft_exec_fourstep_scatter": (_INT, [_P, _P, _P, _P, _I64, _I64, _INT, _I64, _INT,
                                             ctypes.POINTER(_P), ctypes.POINTER(_P), _I64, _I64, _I64, _P, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
+    "trnfft_plan_enable_f64": (_INT, [_P]),
+    "trnfft_plan_query_f64": (_INT, [_P, _I64, ctypes.POINTER(_I64)]),
+    "trnfft_exec_c2c_f64": (_INT, [_P, _P, _P, _P, _P, _I64, _INT, _P, _P]),
+    "trnfft_convert_f32_f64": (_INT, [_P, _P, _I64, _INT, _INT, _P]),
     "trnfft_exec_istft": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _INT, _INT, _INT, _I64, _P, _P]),
     "trnfft_complex_mask_apply": (_INT, [_P, _P, _I64, _P, _P, _P, _P, _I64, _INT, _P]),
     "trnfft_exec_c2r": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
@@ -145,6 +149,17 @@ class DevicePlan:
         call("trnfft_plan_query", h, ctypes.byref(alg), ctypes.byref(pn), 0, None)
         self.algorithm = alg.value
         self.padded_n = pn.value
+
+    def enable_f64(self) -> None:
+        """Build the plan's fp64 tables (once)."""
+        if not getattr(self, "_f64", False):
+            call("trnfft_plan_enable_f64", self.handle)
+            self._f64 = True
+
+    def work_bytes_f64(self, batch: int) -> int:
+        wb = ctypes.c_int64()
+        call("trnfft_plan_query_f64", self.handle, int(batch), ctypes.byref(wb))
+        return wb.value
 
     def work_bytes(self, batch: int) -> int:
         wb = ctypes.c_int64()

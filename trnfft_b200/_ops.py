@@ -23,11 +23,61 @@ def _flat(t: torch.Tensor, n: int) -> torch.Tensor:
     return t.reshape(-1, n)
 
 
-def _check(t: torch.Tensor, what: str) -> None:
+def _check(t: torch.Tensor, what: str, f64_ok: bool = False) -> None:
     if not t.is_cuda:
         raise RuntimeError(f"trnfft_b200: {what} must be a CUDA tensor")
-    if t.dtype != torch.float32:
+    if t.dtype != torch.float32 and not (f64_ok and t.dtype == torch.float64):
         raise TypeError(f"trnfft_b200: {what} must be float32, got {t.dtype}")
+
+
+# ---------------------------------------------------------------------------
+# double precision (precision="double", or float64 tensors)
+# ---------------------------------------------------------------------------
+
+
+def _f64_wanted(t: torch.Tensor, precision=None) -> bool:
+    """fp64 kernels run for float64 tensors and, in precision="double", for float32 ones
+    (every size: the reference promotes Bluestein to float64 and runs power-of-two sizes up
+    to 1024 as an fp64 DFT, trnfft/fft_core.py:1108-1110, 1306-1309)."""
+    from .precision import _resolve
+
+    return t.dtype == torch.float64 or _resolve(precision) == "double"
+
+
+def _convert(src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """float32 <-> float64 copy on the library's conversion kernel."""
+    src = src.contiguous()
+    out = torch.empty(src.shape, dtype=dtype, device=src.device)
+    if src.numel():
+        _lib.call("trnfft_convert_f32_f64", _lib.ptr(src), _lib.ptr(out), src.numel(),
+                  int(dtype == torch.float64), src.device.index, _lib.stream_ptr(src.device))
+    return out
+
+
+def c2c_f64_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool):
+    """Transform along the last axis with every stage in fp64 (trnfft_exec_c2c_f64).
+    float32 inputs are widened on the device and the result narrowed back."""
+    _check(xr, "real part", True)
+    _check(xi, "imaginary part", True)
+    n = xr.shape[-1]
+    shape, odt = xr.shape, xr.dtype
+    a = _flat(xr, n)
+    b = _flat(xi.to(odt), n)
+    if odt != torch.float64:
+        a, b = _convert(a, torch.float64), _convert(b, torch.float64)
+    batch = a.shape[0]
+    yr = torch.empty_like(a)
+    yi = torch.empty_like(b)
+    if batch and n:
+        plan = _lib.device_plan(n, a.device)
+        plan.enable_f64()
+        wb = plan.work_bytes_f64(batch)
+        work = torch.empty(wb, dtype=torch.uint8, device=a.device) if wb else None
+        _lib.call("trnfft_exec_c2c_f64", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi), batch,
+                  int(bool(inverse)), _lib.ptr(work), _lib.stream_ptr(a.device))
+    if odt != torch.float64:
+        yr, yi = _convert(yr, odt), _convert(yi, odt)
+    return yr.reshape(shape), yi.reshape(shape)
 
 
 # ---------------------------------------------------------------------------
@@ -63,7 +113,9 @@ def dft_gemm_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool):
     return yr.reshape(shape), yi.reshape(shape)
 
 
-def c2c_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool) -> tuple[torch.Tensor, torch.Tensor]:
+def c2c_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool, precision=None) -> tuple[torch.Tensor, torch.Tensor]:
+    if _f64_wanted(xr, precision):
+        return c2c_f64_raw(xr, xi, inverse)
     _check(xr, "real part")
     _check(xi, "imaginary part")
     n = xr.shape[-1]
@@ -153,10 +205,13 @@ def _real_kernel(n: int, device: torch.device) -> bool:
 
 def r2c_raw(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """rfft along the last axis: (..., n) real -> (..., n//2+1) complex."""
-    _check(x, "input")
     n = x.shape[-1]
     h = n // 2 + 1
     lead = x.shape[:-1]
+    if _f64_wanted(x):  # a complex fp64 transform of the real row, as the reference does (api.py:38-46)
+        yr, yi = c2c_f64_raw(x, torch.zeros_like(x), False)
+        return yr[..., :h].contiguous(), yi[..., :h].contiguous()
+    _check(x, "input")
     a = _flat(x, n)
     batch = a.shape[0]
     if not _real_kernel(n, a.device):
@@ -196,6 +251,10 @@ def hermitian_extend(xr: torch.Tensor, xi: torch.Tensor, n: int):
 
 def c2r_raw(xr: torch.Tensor, xi: torch.Tensor, n: int) -> torch.Tensor:
     """irfft along the last axis: (..., h) complex -> (..., n) real."""
+    if _f64_wanted(xr):
+        fr, fi = hermitian_extend(xr, xi, n)
+        yr, _ = c2c_f64_raw(fr, fi, True)
+        return yr
     _check(xr, "real part")
     _check(xi, "imaginary part")
     h = xr.shape[-1]
@@ -222,10 +281,11 @@ def c2r_raw(xr: torch.Tensor, xi: torch.Tensor, n: int) -> torch.Tensor:
 
 class _C2C(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, xr, xi, inverse: bool):
+    def forward(ctx, xr, xi, inverse: bool, precision=None):
         ctx.inverse = inverse
         ctx.n = xr.shape[-1]
-        return c2c_raw(xr, xi, inverse)
+        ctx.precision = precision
+        return c2c_raw(xr, xi, inverse, precision)
 
     @staticmethod
     def backward(ctx, gr, gi):
@@ -233,12 +293,12 @@ class _C2C(torch.autograd.Function):
         gr = torch.zeros_like(gr) if gr is None else gr
         gi = torch.zeros_like(gi) if gi is None else gi
         if ctx.inverse:
-            dr, di = c2c_raw(gr, gi, False)
+            dr, di = c2c_raw(gr, gi, False, ctx.precision)
             s = 1.0 / n
         else:
-            dr, di = c2c_raw(gr, gi, True)
+            dr, di = c2c_raw(gr, gi, True, ctx.precision)
             s = float(n)
-        return dr * s, di * s, None
+        return dr * s, di * s, None, None
 
 
 class _R2C(torch.autograd.Function):
@@ -291,16 +351,16 @@ def _needs_grad(*ts) -> bool:
     return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in ts)
 
 
-def c2c(xr, xi, inverse: bool):
+def c2c(xr, xi, inverse: bool, precision=None):
     if _needs_grad(xr, xi):
-        return _C2C.apply(xr, xi, inverse)
-    return c2c_raw(xr, xi, inverse)
+        return _C2C.apply(xr, xi, inverse, precision)
+    return c2c_raw(xr, xi, inverse, precision)
 
 
 def r2c(x):
     if _needs_grad(x):
         n = x.shape[-1]
-        if x.is_cuda and _real_kernel(n, x.device):
+        if x.is_cuda and not _f64_wanted(x) and _real_kernel(n, x.device):
             return _R2C.apply(x)
         h = n // 2 + 1
         yr, yi = _C2C.apply(x, torch.zeros_like(x), False)
@@ -310,7 +370,7 @@ def r2c(x):
 
 def c2r(xr, xi, n: int):
     if _needs_grad(xr, xi):
-        if xr.is_cuda and xr.shape[-1] == n // 2 + 1 and _real_kernel(n, xr.device):
+        if xr.is_cuda and not _f64_wanted(xr) and xr.shape[-1] == n // 2 + 1 and _real_kernel(n, xr.device):
             return _C2R.apply(xr, xi, n)
         fr, fi = hermitian_extend(xr, xi, n)
         yr, _ = _C2C.apply(fr, fi, True)

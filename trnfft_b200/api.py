@@ -265,7 +265,10 @@ def _fft_along_dim(x: ComplexTensor, dim: int, inverse: bool) -> ComplexTensor:
     if dim == ndim - 1:
         return fft_core(x, inverse=inverse)
     n = x.shape[dim]
-    if n > 1 and _ops.axis_supported(n):
+    from .precision import get_precision
+
+    f64 = x.real.dtype == torch.float64 or get_precision() == "double"
+    if n > 1 and _ops.axis_supported(n) and not f64:  # the strided-axis kernels are float32
         (xr, xi), restore = place(x.real, x.imag)
         yr, yi = _ops.c2c_axis(xr, xi, dim, bool(inverse))
         return ComplexTensor(restore(yr), restore(yi))

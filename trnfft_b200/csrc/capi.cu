@@ -57,6 +57,13 @@ int ensure_device_tables(int device) {
   }
   cudaError_t e = cudaMemcpyToSymbol(g_tw, h.data(), sizeof(float2) * kTwN);
   if (e != cudaSuccess) return cuda_fail(e, "uploading twiddle table");
+  std::vector<double2> h64(4096);
+  for (int i = 0; i < 4096; ++i) {
+    const double a = -2.0 * M_PI * (double)i / 4096.0;
+    h64[i] = make_double2(std::cos(a), std::sin(a));
+  }
+  e = upload_tw64(h64.data());
+  if (e != cudaSuccess) return cuda_fail(e, "uploading the double-precision twiddle table");
   g_dev_ready[device] = true;
   return TRNFFT_SUCCESS;
 }
@@ -426,6 +433,151 @@ static int make_large_bluestein(trnfft_plan_s* p) {
   return TRNFFT_SUCCESS;
 }
 
+
+// ---- double precision ------------------------------------------------------
+
+static constexpr int kMaxF64Log = 24;        // power-of-two fp64 transforms up to 2^24 (two passes)
+static constexpr int kMaxF64BlockLog = 12;   // one pass up to 4096 points
+
+static std::mutex g_f64_mu;
+
+template <class T>
+static cudaError_t upload_new(T** dst, const std::vector<T>& h) {
+  cudaError_t e = cudaMalloc(dst, sizeof(T) * h.size());
+  if (e == cudaSuccess) e = cudaMemcpy(*dst, h.data(), sizeof(T) * h.size(), cudaMemcpyHostToDevice);
+  return e;
+}
+
+// Tables of plan p for fp64 execution (its device current, g_f64_mu held).
+static int enable_f64_locked(trnfft_plan_s* p) {
+  if (p->f64) return TRNFFT_SUCCESS;
+  cudaError_t e = cudaSuccess;
+  if (p->algorithm == TRNFFT_ALG_STOCKHAM || p->algorithm == TRNFFT_ALG_MULTIPASS) {
+    if (p->logn > kMaxF64Log)
+      return fail(TRNFFT_UNSUPPORTED, "double precision: n=2^%d above the supported 2^%d", p->logn, kMaxF64Log);
+    if (p->logn > kMaxF64BlockLog) {
+      const int L = p->logn, sp = (L + 1) / 2;
+      std::vector<double2> lo(size_t(1) << sp), hi(size_t(1) << (L - sp));
+      const double n = std::ldexp(1.0, L);
+      for (size_t i = 0; i < lo.size(); ++i) {
+        const double a = -2.0 * M_PI * (double)i / n;
+        lo[i] = make_double2(std::cos(a), std::sin(a));
+      }
+      for (size_t i = 0; i < hi.size(); ++i) {
+        const double a = -2.0 * M_PI * (double)(i << sp) / n;
+        hi[i] = make_double2(std::cos(a), std::sin(a));
+      }
+      e = upload_new(&p->tw64_lo, lo);
+      if (e == cudaSuccess) e = upload_new(&p->tw64_hi, hi);
+      p->tw64_split = sp;
+    }
+  } else if (p->algorithm == TRNFFT_ALG_BLUESTEIN) {
+    const int64_t n = p->n, m = p->m;
+    if (p->logm > kMaxF64Log)
+      return fail(TRNFFT_UNSUPPORTED, "double precision: Bluestein n=%lld (padded 2^%d) above 2^%d", (long long)n,
+                  p->logm, kMaxF64Log);
+    std::vector<double2> c(n), hf(m);
+    std::vector<std::complex<double>> h(m, 0.0);
+    for (int64_t k = 0; k < n; ++k) {
+      const int64_t ex = (k * k) % (2 * n);
+      const double ang = -M_PI * (double)ex / (double)n;
+      c[k] = make_double2(std::cos(ang), std::sin(ang));
+    }
+    for (int64_t j = 0; j < n; ++j) h[j] = std::complex<double>(c[j].x, -c[j].y);
+    for (int64_t j = 1; j < n; ++j) h[m - j] = std::complex<double>(c[j].x, -c[j].y);
+    host_fft_double(h);
+    for (int64_t k = 0; k < m; ++k) hf[k] = make_double2(h[k].real() / (double)m, h[k].imag() / (double)m);
+    e = upload_new(&p->chirp64, c);
+    if (e == cudaSuccess) e = upload_new(&p->H64, hf);
+    if (e == cudaSuccess) {
+      trnfft_plan_t sub = nullptr;
+      int rc = trnfft_plan_create(&sub, m, p->device);
+      if (rc) return rc;
+      p->sub64 = sub;
+      rc = enable_f64_locked(sub);
+      if (rc) return rc;
+    }
+  }
+  if (e != cudaSuccess) return fail(TRNFFT_ALLOC_FAILED, "double precision tables: %s", cudaGetErrorString(e));
+  p->f64 = true;
+  return TRNFFT_SUCCESS;
+}
+
+static int64_t f64_work_bytes(const trnfft_plan_s* p, int64_t batch) {
+  if (p->algorithm == TRNFFT_ALG_BLUESTEIN) {
+    int64_t w = (int64_t)(2 * sizeof(double)) * p->m * batch;
+    if (p->logm > kMaxF64BlockLog) w *= 2;
+    return w;
+  }
+  if (p->algorithm != TRNFFT_ALG_COPY && p->logn > kMaxF64BlockLog) return (int64_t)(2 * sizeof(double)) * p->n * batch;
+  return 0;
+}
+
+// Power-of-two fp64 transform of `batch` contiguous rows; `scale` multiplies the result.
+static cudaError_t run_f64_pow2(const trnfft_plan_s* p, const double* xr, const double* xi, double* yr, double* yi,
+                                int64_t batch, bool inv, double scale, double* work, cudaStream_t st) {
+  const int L = p->logn;
+  const long long N = p->n;
+  F64SeqArgs a;
+  std::memset(&a, 0, sizeof a);
+  if (L <= kMaxF64BlockLog) {
+    a.xr = xr; a.xi = xi; a.yr = yr; a.yi = yi;
+    a.nseq = batch; a.inner = 1;
+    a.in_outer = N; a.in_js = 1;
+    a.out_outer = N; a.out_ks = 1;
+    a.scale = scale;
+    return launch_f64_seq(L, inv, a, st);
+  }
+  // N = N1 * N2, n = n1 N2 + n2, k = k1 + N1 k2:
+  // A: columns n2, FFT over n1 (stride N2), times W_N^{n2 k1} -> work[k1][n2]
+  // B: rows k1 of work, FFT over n2, stored at k1 + N1 k2 (natural order)
+  const int l1 = L / 2, l2 = L - l1;
+  const long long N1 = 1LL << l1, N2 = 1LL << l2;
+  double* wr = work;
+  double* wi = work + (size_t)N * batch;
+  a.xr = xr; a.xi = xi; a.yr = wr; a.yi = wi;
+  a.nseq = batch * N2; a.inner = N2;
+  a.in_outer = N; a.in_cs = 1; a.in_js = N2;
+  a.out_outer = N; a.out_cs = 1; a.out_ks = N2;
+  a.tw_hi = p->tw64_hi; a.tw_lo = p->tw64_lo; a.tw_split = p->tw64_split;
+  a.tw_mask = (unsigned long long)(N - 1); a.tw_off = 0;
+  a.scale = 1.0;
+  cudaError_t e = launch_f64_seq(l1, inv, a, st);
+  if (e != cudaSuccess) return e;
+  F64SeqArgs b;
+  std::memset(&b, 0, sizeof b);
+  b.xr = wr; b.xi = wi; b.yr = yr; b.yi = yi;
+  b.nseq = batch * N1; b.inner = N1;
+  b.in_outer = N; b.in_cs = N2; b.in_js = 1;
+  b.out_outer = N; b.out_cs = 1; b.out_ks = N1;
+  b.scale = scale;
+  return launch_f64_seq(l2, inv, b, st);
+}
+
+static cudaError_t run_f64(const trnfft_plan_s* p, const double* xr, const double* xi, double* yr, double* yi,
+                           int64_t batch, bool inv, double* work, cudaStream_t st) {
+  const double sc = inv ? 1.0 / (double)p->n : 1.0;
+  if (p->algorithm == TRNFFT_ALG_COPY) {
+    const size_t bytes = sizeof(double) * (size_t)batch;
+    cudaError_t e = cudaSuccess;
+    if (yr != xr) e = cudaMemcpyAsync(yr, xr, bytes, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess && yi != xi) e = cudaMemcpyAsync(yi, xi, bytes, cudaMemcpyDeviceToDevice, st);
+    return e;
+  }
+  if (p->algorithm != TRNFFT_ALG_BLUESTEIN) return run_f64_pow2(p, xr, xi, yr, yi, batch, inv, sc, work, st);
+  // Bluestein: chirp premultiply, m-point FFT, times H, unscaled inverse m-point FFT (1/m is in H), postmultiply
+  const long long m = p->m;
+  double* ar = work;
+  double* ai = work + (size_t)m * batch;
+  double* sub_work = work + 2 * (size_t)m * batch;
+  cudaError_t e = launch_f64_blue_pre(xr, xi, p->chirp64, ar, ai, batch, p->n, m, inv, st);
+  if (e == cudaSuccess) e = run_f64_pow2(p->sub64, ar, ai, ar, ai, batch, false, 1.0, sub_work, st);
+  if (e == cudaSuccess) e = launch_f64_blue_mul(ar, ai, p->H64, batch, m, inv, st);
+  if (e == cudaSuccess) e = run_f64_pow2(p->sub64, ar, ai, ar, ai, batch, true, 1.0, sub_work, st);
+  if (e == cudaSuccess) e = launch_f64_blue_post(ar, ai, p->chirp64, yr, yi, batch, p->n, m, inv, sc, st);
+  return e;
+}
+
 extern "C" {
 
 int trnfft_abi_version(void) { return TRNFFT_B200_ABI_VERSION; }
@@ -516,6 +668,14 @@ int trnfft_plan_destroy(trnfft_plan_t plan) {
     if (plan->Hr) cudaFree(plan->Hr);
     if (plan->Hi) cudaFree(plan->Hi);
   }
+  if (plan->tw64_hi || plan->tw64_lo || plan->chirp64 || plan->H64) {
+    DeviceGuard g(plan->device);
+    if (plan->tw64_hi) cudaFree(plan->tw64_hi);
+    if (plan->tw64_lo) cudaFree(plan->tw64_lo);
+    if (plan->chirp64) cudaFree(plan->chirp64);
+    if (plan->H64) cudaFree(plan->H64);
+  }
+  if (plan->sub64) trnfft_plan_destroy(plan->sub64);
   if (plan->sub) trnfft_plan_destroy(plan->sub);
   delete plan;
   return TRNFFT_SUCCESS;
@@ -1019,6 +1179,60 @@ int trnfft_complex_mask_apply(const float* mask_re, const float* mask_im, int64_
   cudaError_t e = launch_cmul(mask_re, mask_im, mask_count, spec_re, spec_im, out_re, out_im, count,
                               reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "complex_mask_apply");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_plan_enable_f64(trnfft_plan_t plan) {
+  if (!plan) return fail(TRNFFT_INVALID_VALUE, "plan_enable_f64: null plan");
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "plan_enable_f64: cannot select device %d", plan->device);
+  std::lock_guard<std::mutex> lk(g_f64_mu);
+  return enable_f64_locked(plan);
+}
+
+int trnfft_plan_query_f64(trnfft_plan_t plan, int64_t batch, int64_t* work_bytes) {
+  if (!plan || !work_bytes || batch < 0) return fail(TRNFFT_INVALID_VALUE, "plan_query_f64: bad arguments");
+  *work_bytes = f64_work_bytes(plan, batch);
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_exec_c2c_f64(trnfft_plan_t plan, const double* in_re, const double* in_im, double* out_re,
+                        double* out_im, int64_t batch, int inverse, void* work, void* stream) {
+  if (!plan) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64: null plan");
+  if (batch < 0) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64: negative batch");
+  if (!plan->f64) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64: call trnfft_plan_enable_f64 on the plan first");
+  if (batch == 0) return TRNFFT_SUCCESS;
+  int rc = check_ptrs("exec_c2c_f64", {in_re, in_im, out_re, out_im}, 8);
+  if (rc) return rc;
+  const size_t cnt = (size_t)plan->n * (size_t)batch;
+  const size_t b = cnt * sizeof(double);
+  const bool partial = (ranges_overlap(in_re, b, out_re, b) || ranges_overlap(in_re, b, out_im, b) ||
+                        ranges_overlap(in_im, b, out_re, b) || ranges_overlap(in_im, b, out_im, b)) &&
+                       !(in_re == out_re && in_im == out_im);
+  if (partial) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64: input and output planes partly overlap");
+  const int64_t wb = f64_work_bytes(plan, batch);
+  if (wb > 0) {
+    if (!work) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64: n=%lld needs a work area of %lld bytes",
+                           (long long)plan->n, (long long)wb);
+    if (!aligned(work, 16)) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64: work area not 16-byte aligned");
+  }
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_c2c_f64: cannot select device %d", plan->device);
+  cudaError_t e = run_f64(plan, in_re, in_im, out_re, out_im, batch, inverse != 0, static_cast<double*>(work),
+                          reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_f64");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_convert_f32_f64(const void* src, void* dst, int64_t count, int to_double, int device, void* stream) {
+  if (count < 0 || (count && (!src || !dst))) return fail(TRNFFT_INVALID_VALUE, "convert_f32_f64: bad arguments");
+  if (count == 0) return TRNFFT_SUCCESS;
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "convert_f32_f64: cannot select device %d", device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = to_double ? launch_f32_to_f64(static_cast<const float*>(src), static_cast<double*>(dst), count, st)
+                            : launch_f64_to_f32(static_cast<const double*>(src), static_cast<float*>(dst), count, st);
+  if (e != cudaSuccess) return cuda_fail(e, "convert_f32_f64");
   return TRNFFT_SUCCESS;
 }
 

@@ -119,6 +119,39 @@ struct IstftArgs {
 
 cudaError_t launch_istft(int logn, const IstftArgs& a, cudaStream_t st);
 
+// Double-precision sequence transforms (f64.cu): nseq sequences of 2^logl
+// points; sequence s starts at (s / inner) * outer + (s % inner) * cs and its
+// points are js apart (in_* for the input, out_* / ks for the output).  With
+// tw_hi set, output k of sequence s is multiplied by W^e, e = ((s % inner) +
+// tw_off) * k & tw_mask, from the two-level table hi[e >> split] * lo[e & ...].
+struct F64SeqArgs {
+  const double* xr;
+  const double* xi;
+  double* yr;
+  double* yi;
+  long long nseq, inner;
+  long long in_outer, in_cs, in_js;
+  long long out_outer, out_cs, out_ks;
+  const double2* tw_hi;
+  const double2* tw_lo;
+  int tw_split;
+  unsigned long long tw_mask;
+  long long tw_off;
+  double scale;
+};
+
+cudaError_t launch_f64_seq(int logl, bool inv, const F64SeqArgs& a, cudaStream_t st);
+cudaError_t launch_f64_blue_pre(const double* xr, const double* xi, const double2* chirp, double* ar, double* ai,
+                                long long batch, long long n, long long m, bool inv, cudaStream_t st);
+cudaError_t launch_f64_blue_mul(double* ar, double* ai, const double2* H, long long batch, long long m, bool inv,
+                                cudaStream_t st);
+cudaError_t launch_f64_blue_post(const double* ar, const double* ai, const double2* chirp, double* yr, double* yi,
+                                 long long batch, long long n, long long m, bool inv, double scale, cudaStream_t st);
+cudaError_t launch_f32_to_f64(const float* x, double* y, long long count, cudaStream_t st);
+cudaError_t launch_f64_to_f32(const double* x, float* y, long long count, cudaStream_t st);
+// Upload W_4096^i in double to the current device (f64.cu), once per device.
+cudaError_t upload_tw64(const double2* host_table);
+
 // Element-wise complex product y = m[i mod mcount] * s[i] (mask.cu), i < count.
 cudaError_t launch_cmul(const float* mr, const float* mi, long long mcount, const float* sr, const float* si,
                         float* yr, float* yi, long long count, cudaStream_t st);

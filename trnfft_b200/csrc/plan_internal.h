@@ -22,4 +22,14 @@ struct trnfft_plan_s {
   struct trnfft_plan_s* sub = nullptr;
   float* Hr = nullptr;
   float* Hi = nullptr;
+  // double precision (trnfft_plan_enable_f64): power of two n > 4096: two-level
+  // table of W_n; Bluestein: chirp and H = FFT_m(h)/m in double, and an m-point
+  // sub-plan (also fp64-enabled) for the padded transforms
+  bool f64 = false;
+  double2* tw64_hi = nullptr;
+  double2* tw64_lo = nullptr;
+  int tw64_split = 0;
+  double2* chirp64 = nullptr;
+  double2* H64 = nullptr;
+  struct trnfft_plan_s* sub64 = nullptr;
 };

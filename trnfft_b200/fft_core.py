@@ -37,21 +37,21 @@ def fft_core(
         plan = create_plan(n, inverse=inverse)
     if plan.n != n:
         raise ValueError(f"plan is for n={plan.n}, input has n={n}")
-    (xr, xi), restore = place(x.real, x.imag)
+    (xr, xi), restore = place(x.real, x.imag, allow_f64=True)
     if n == 0 or xr.numel() == 0:
         return ComplexTensor(restore(xr.clone()), restore(xi.clone()))
-    yr, yi = _ops.c2c(xr, xi, bool(inverse))
+    yr, yi = _ops.c2c(xr, xi, bool(inverse), precision=_resolve(precision))
     return ComplexTensor(restore(yr), restore(yi))
 
 
 def rfft_core(x: torch.Tensor) -> ComplexTensor:
     """Real-input transform along the last dimension, n//2+1 bins."""
-    (xd,), restore = place(x)
+    (xd,), restore = place(x, allow_f64=True)
     yr, yi = _ops.r2c(xd)
     return ComplexTensor(restore(yr), restore(yi))
 
 
 def irfft_core(x: ComplexTensor, n: int) -> torch.Tensor:
     """Real result of the inverse transform of the Hermitian extension of ``x``."""
-    (xr, xi), restore = place(x.real, x.imag)
+    (xr, xi), restore = place(x.real, x.imag, allow_f64=True)
     return restore(_ops.c2r(xr, xi, n))

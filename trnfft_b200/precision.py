@@ -8,9 +8,13 @@
   it is rounded, so the float32 pipeline reaches about 4e-7 instead of the
   reference's 1e-4 (its float32 angle pi*k*k/n, trnfft/fft_core.py:1316-1320,
   loses ~1e-3 rad at k ~ 4000).
-* ``"double"``: the reference promotes Bluestein to float64 for accuracy
-  (fft_core.py:1306-1309).  The float32 exact-chirp kernels already land
-  within 1e-6 of that result, so they serve this mode too.
+* ``"double"``: every transform runs the fp64 kernels (trnfft_exec_c2c_f64:
+  twiddles, chirp, filter spectrum and butterflies in float64; float32 data is
+  widened on the device and the result rounded back).  The reference promotes
+  Bluestein to float64 (fft_core.py:1306-1309) and runs power-of-two sizes up
+  to 1024 as an fp64 DFT (fft_core.py:1108-1110); here every size gets fp64,
+  which is at least as accurate.  float64 tensors always take the fp64
+  kernels and come back float64, as with the reference's torch backend.
 
 The remaining modes (``"kahan"``, ``"bf16"``, ``"bf16_refined"``, ``"ozaki"``,
 ``"ozaki_hq"``) are Trainium PSUM-precision experiments of the reference
