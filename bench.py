@@ -224,7 +224,12 @@ class C2CRoundTrip(Workload):
         self.name = f"batched C2C FFT+IFFT round trip, N={n}, batch={batch} per GPU ({tag})"
         self.work = 2 * c2c_flops(n, batch)
         self.dom_bytes = 16.0 * n * batch
-        alg = "Stockham" if n & (n - 1) == 0 else "fused Bluestein"
+        smooth = n
+        for f in (2, 3, 5, 7):
+            while smooth % f == 0:
+                smooth //= f
+        alg = ("Stockham" if n & (n - 1) == 0 else
+               ("direct mixed-radix" if smooth == 1 and n <= 8192 else "fused Bluestein"))
         self.dominant = f"{alg} C2C kernel, N={n}"
 
     def setup(self, dev, g):

@@ -57,7 +57,8 @@ typedef enum {
   TRNFFT_ALG_COPY = 0,      /* n == 1 */
   TRNFFT_ALG_STOCKHAM = 1,  /* power of two, n <= 4096: one pass over HBM */
   TRNFFT_ALG_MULTIPASS = 2, /* power of two, n > 4096: one pass up to 16384, else 2-4 passes */
-  TRNFFT_ALG_BLUESTEIN = 3  /* any other n: fused chirp-z, one pass over HBM */
+  TRNFFT_ALG_BLUESTEIN = 3, /* any other n: fused chirp-z, one pass over HBM */
+  TRNFFT_ALG_MIXED = 4      /* 7-smooth n <= 8192 (not a power of two): direct mixed-radix, one pass */
 } trnfft_algorithm;
 
 typedef struct trnfft_plan_s* trnfft_plan_t;

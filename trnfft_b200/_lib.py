@@ -24,7 +24,7 @@ UNSUPPORTED = 2
 CUDA_ERROR = 3
 ALLOC_FAILED = 4
 
-ALG_COPY, ALG_STOCKHAM, ALG_MULTIPASS, ALG_BLUESTEIN = 0, 1, 2, 3
+ALG_COPY, ALG_STOCKHAM, ALG_MULTIPASS, ALG_BLUESTEIN, ALG_MIXED = 0, 1, 2, 3, 4
 
 _lib = None
 _lib_lock = threading.Lock()

@@ -193,13 +193,16 @@ def _r2c_native(n: int) -> bool:
 
 def _real_kernel(n: int, device: torch.device) -> bool:
     """Whether trnfft_exec_r2c / _c2r have a direct kernel for n on this device:
-    powers of two 4..8192 (packed real rows) and Bluestein lengths whose padded
-    size m fits one block (m <= 16384, the fused kernel's real-input modes)."""
+    powers of two 4..8192 (packed real rows), 7-smooth lengths up to 8192 (the
+    mixed-radix kernel's real modes) and Bluestein lengths whose padded size m
+    fits one block (m <= 16384, the fused kernel's real-input modes)."""
     if _r2c_native(n):
         return True
     if n < 3 or (n & (n - 1)) == 0:
         return False
     plan = _lib.device_plan(n, device)
+    if plan.algorithm == _lib.ALG_MIXED:
+        return True
     return plan.algorithm == _lib.ALG_BLUESTEIN and plan.padded_n <= 16384
 
 

@@ -15,6 +15,8 @@
 //     inverse m-point FFT -> postmultiply, so x is read once and X written once.
 // The inverse transform uses conj(chirp) and H_inv[k] = conj(H[(m-k) mod m])
 // (FFT of conj(h)), and scales by 1/n (fft_core.py:1369-1370).
+#include <cstdlib>
+
 #include "fft_common.cuh"
 #include "kernels.h"
 
@@ -27,9 +29,9 @@ struct BlueLogE {
   static constexpr int v = LOGM >= 13 ? 5 : 4;  // m >= 8192: radix-32 (measured faster there)
 };
 
-template <int LOGM>
+template <int LOGM, int LE_ = BlueLogE<LOGM>::v>
 struct BlueGeom {
-  static constexpr int LE = BlueLogE<LOGM>::v;
+  static constexpr int LE = LE_;
   using S = Sched<LOGM, LE>;
   static constexpr int THREADS = S::T > 128 ? S::T : 128;
   // <= 128 registers per thread for the radix-16 kernels; the radix-32 ones keep all they need
@@ -40,9 +42,9 @@ struct BlueGeom {
 };
 
 // MODE 0: C2C, MODE 1: R2C (real rows -> n/2+1 bins), MODE 2: C2R (n/2+1 bins -> real rows)
-template <int LOGM, bool INV, int MODE>
-__global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS, BlueGeom<LOGM>::MINB) k_bluestein(BlueArgs a) {
-  using GM = BlueGeom<LOGM>;
+template <int LOGM, bool INV, int MODE, int LE_ = BlueLogE<LOGM>::v>
+__global__ void __launch_bounds__(BlueGeom<LOGM, LE_>::THREADS, BlueGeom<LOGM, LE_>::MINB) k_bluestein(BlueArgs a) {
+  using GM = BlueGeom<LOGM, LE_>;
   constexpr int LE = GM::LE;
   using S = Sched<LOGM, LE>;
   constexpr int M = S::N;
@@ -143,10 +145,10 @@ __global__ void __launch_bounds__(BlueGeom<LOGM>::THREADS, BlueGeom<LOGM>::MINB)
   });
 }
 
-template <int LOGM, bool INV, int MODE>
+template <int LOGM, bool INV, int MODE, int LE_ = BlueLogE<LOGM>::v>
 static cudaError_t launch_blue_t(const BlueArgs& a, cudaStream_t st) {
-  using GM = BlueGeom<LOGM>;
-  auto kern = k_bluestein<LOGM, INV, MODE>;
+  using GM = BlueGeom<LOGM, LE_>;
+  auto kern = k_bluestein<LOGM, INV, MODE, LE_>;
   if (GM::smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
     if (e != cudaSuccess) return e;
@@ -156,8 +158,28 @@ static cudaError_t launch_blue_t(const BlueArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// TRNFFT_B200_BLUE_LOGE=4 runs the m >= 8192 sizes with 16 values per thread
+// (twice the threads, half the registers each) for measurement.
+static int blue_loge_override() {
+  static const int v = [] {
+    const char* e = getenv("TRNFFT_B200_BLUE_LOGE");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
 template <int LOGM>
 static cudaError_t launch_blue_m(int mode, bool inv, const BlueArgs& a, cudaStream_t st) {
+  if constexpr (LOGM >= 13) {
+    if (blue_loge_override() == 4) {
+      switch (mode) {
+        case 0: return inv ? launch_blue_t<LOGM, true, 0, 4>(a, st) : launch_blue_t<LOGM, false, 0, 4>(a, st);
+        case 1: return launch_blue_t<LOGM, false, 1, 4>(a, st);
+        case 2: return launch_blue_t<LOGM, true, 2, 4>(a, st);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+  }
   switch (mode) {
     case 0: return inv ? launch_blue_t<LOGM, true, 0>(a, st) : launch_blue_t<LOGM, false, 0>(a, st);
     case 1: return launch_blue_t<LOGM, false, 1>(a, st);

@@ -471,7 +471,7 @@ static int enable_f64_locked(trnfft_plan_s* p) {
       if (e == cudaSuccess) e = upload_new(&p->tw64_hi, hi);
       p->tw64_split = sp;
     }
-  } else if (p->algorithm == TRNFFT_ALG_BLUESTEIN) {
+  } else if (p->algorithm == TRNFFT_ALG_BLUESTEIN || p->algorithm == TRNFFT_ALG_MIXED) {
     const int64_t n = p->n, m = p->m;
     if (p->logm > kMaxF64Log)
       return fail(TRNFFT_UNSUPPORTED, "double precision: Bluestein n=%lld (padded 2^%d) above 2^%d", (long long)n,
@@ -504,7 +504,7 @@ static int enable_f64_locked(trnfft_plan_s* p) {
 }
 
 static int64_t f64_work_bytes(const trnfft_plan_s* p, int64_t batch) {
-  if (p->algorithm == TRNFFT_ALG_BLUESTEIN) {
+  if (p->algorithm == TRNFFT_ALG_BLUESTEIN || p->algorithm == TRNFFT_ALG_MIXED) {
     int64_t w = (int64_t)(2 * sizeof(double)) * p->m * batch;
     if (p->logm > kMaxF64BlockLog) w *= 2;
     return w;
@@ -564,7 +564,8 @@ static cudaError_t run_f64(const trnfft_plan_s* p, const double* xr, const doubl
     if (e == cudaSuccess && yi != xi) e = cudaMemcpyAsync(yi, xi, bytes, cudaMemcpyDeviceToDevice, st);
     return e;
   }
-  if (p->algorithm != TRNFFT_ALG_BLUESTEIN) return run_f64_pow2(p, xr, xi, yr, yi, batch, inv, sc, work, st);
+  if (p->algorithm != TRNFFT_ALG_BLUESTEIN && p->algorithm != TRNFFT_ALG_MIXED)
+    return run_f64_pow2(p, xr, xi, yr, yi, batch, inv, sc, work, st);
   // Bluestein: chirp premultiply, m-point FFT, times H, unscaled inverse m-point FFT (1/m is in H), postmultiply
   const long long m = p->m;
   double* ar = work;
@@ -576,6 +577,58 @@ static cudaError_t run_f64(const trnfft_plan_s* p, const double* xr, const doubl
   if (e == cudaSuccess) e = run_f64_pow2(p->sub64, ar, ai, ar, ai, batch, true, 1.0, sub_work, st);
   if (e == cudaSuccess) e = launch_f64_blue_post(ar, ai, p->chirp64, yr, yi, batch, p->n, m, inv, sc, st);
   return e;
+}
+
+// Mixed-radix schedule of n (radices 16, 8, 4, 2, then 3, 5, 7), or 0 passes when
+// n has another prime factor.  Larger power-of-two radices first: fewer passes.
+static int mixed_schedule(int64_t n, int* radix) {
+  int np = 0;
+  int64_t v = n;
+  while (v % 16 == 0 && np < 16) { radix[np++] = 16; v /= 16; }
+  while (v % 8 == 0 && np < 16) { radix[np++] = 8; v /= 8; }
+  while (v % 4 == 0 && np < 16) { radix[np++] = 4; v /= 4; }
+  while (v % 2 == 0 && np < 16) { radix[np++] = 2; v /= 2; }
+  for (int r : {5, 3, 7})
+    while (v % r == 0 && np < 16) { radix[np++] = r; v /= r; }
+  return v == 1 ? np : 0;
+}
+
+static constexpr int64_t kMaxMixedN = 8192;
+
+// Mixed-radix plan tables: pass by pass, W_{ns R}^{k r} for k < ns, 1 <= r < R
+// ([k][r-1]), computed in double and rounded once; and the packed radix codes.
+static int mixed_code(int r) {
+  switch (r) {
+    case 2: return 0;
+    case 3: return 1;
+    case 4: return 2;
+    case 5: return 3;
+    case 7: return 4;
+    case 8: return 5;
+    default: return 6;  // 16
+  }
+}
+
+static int make_mixed_tables(trnfft_plan_s* p) {
+  std::vector<float2> t;
+  long long ns = 1;
+  p->codes = 0;
+  for (int q = 0; q < p->npass; ++q) {
+    const int R = p->radix[q];
+    p->codes |= (unsigned long long)mixed_code(R) << (3 * q);
+    for (long long k = 0; k < ns; ++k)
+      for (int r = 1; r < R; ++r) {
+        const long long e = (k * r) % (ns * R);
+        const double a = -2.0 * M_PI * (double)e / (double)(ns * R);
+        t.push_back(make_float2((float)std::cos(a), (float)std::sin(a)));
+      }
+    ns *= R;
+  }
+  if (t.empty()) t.push_back(make_float2(1.f, 0.f));
+  cudaError_t e = cudaMalloc(&p->twn, sizeof(float2) * t.size());
+  if (e == cudaSuccess) e = cudaMemcpy(p->twn, t.data(), sizeof(float2) * t.size(), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail(TRNFFT_ALLOC_FAILED, "plan_create: mixed-radix table: %s", cudaGetErrorString(e));
+  return TRNFFT_SUCCESS;
 }
 
 extern "C" {
@@ -607,8 +660,23 @@ int trnfft_plan_create(trnfft_plan_t* plan, int64_t n, int device) {
     p->algorithm = TRNFFT_ALG_STOCKHAM;
   } else if (p->logn > 12) {
     p->algorithm = TRNFFT_ALG_MULTIPASS;
+  } else if (n <= kMaxMixedN && (p->npass = mixed_schedule(n, p->radix)) > 0 &&
+             !getenv("TRNFFT_B200_NO_MIXED")) {
+    // 7-smooth: direct mixed radix (the Bluestein length is kept for the fp64 path)
+    p->algorithm = TRNFFT_ALG_MIXED;
+    int64_t v = 2 * n - 2;
+    int bl = 0;
+    while (v >> bl) ++bl;
+    p->m = int64_t(1) << bl;
+    p->logm = bl;
+    int rc2 = make_mixed_tables(p);
+    if (rc2) {
+      trnfft_plan_destroy(p);
+      return rc2;
+    }
   } else {
     p->algorithm = TRNFFT_ALG_BLUESTEIN;
+    p->npass = 0;
     int64_t v = 2 * n - 2;
     int bl = 0;
     while (v >> bl) ++bl;
@@ -667,6 +735,10 @@ int trnfft_plan_destroy(trnfft_plan_t plan) {
     if (plan->tw_lo) cudaFree(plan->tw_lo);
     if (plan->Hr) cudaFree(plan->Hr);
     if (plan->Hi) cudaFree(plan->Hi);
+  }
+  if (plan->twn) {
+    DeviceGuard g(plan->device);
+    cudaFree(plan->twn);
   }
   if (plan->tw64_hi || plan->tw64_lo || plan->chirp64 || plan->H64) {
     DeviceGuard g(plan->device);
@@ -795,6 +867,17 @@ int trnfft_exec_c2c(trnfft_plan_t plan, const float* in_re, const float* in_im, 
         xi = w + cnt;
       }
       e = run_rows_multipass(plan, xr, xi, out_re, out_im, batch, inverse != 0, st);
+      break;
+    }
+    case TRNFFT_ALG_MIXED: {
+      MixedArgs a;
+      std::memset(&a, 0, sizeof a);
+      a.xr = in_re; a.xi = in_im; a.yr = out_re; a.yi = out_im;
+      a.batch = batch; a.n = (int)n; a.npass = plan->npass;
+      a.codes = plan->codes;
+      a.tw = plan->twn;
+      a.scale = inverse ? (float)(1.0 / (double)n) : 1.f;
+      e = launch_mixed(0, inverse != 0, a, st);
       break;
     }
     case TRNFFT_ALG_BLUESTEIN: {
@@ -1076,6 +1159,17 @@ int trnfft_exec_r2c(trnfft_plan_t plan, const float* in, float* out_re, float* o
     if (rc) return rc;
     RowArgs a{in, nullptr, out_re, out_im, batch, n, n / 2 + 1, 1.0f};
     e = launch_rows_r2c(plan->logn - 1, a, st);
+  } else if (plan->algorithm == TRNFFT_ALG_MIXED) {
+    int rc = check_ptrs("exec_r2c", {in, out_re, out_im}, 4);
+    if (rc) return rc;
+    MixedArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.xr = in; a.yr = out_re; a.yi = out_im;
+    a.batch = batch; a.n = (int)n; a.npass = plan->npass;
+    a.codes = plan->codes;
+    a.tw = plan->twn;
+    a.scale = 1.f;
+    e = launch_mixed(1, false, a, st);
   } else if (plan->algorithm == TRNFFT_ALG_BLUESTEIN && plan->H) {
     int rc = check_ptrs("exec_r2c", {in, out_re, out_im}, 4);
     if (rc) return rc;
@@ -1105,6 +1199,17 @@ int trnfft_exec_c2r(trnfft_plan_t plan, const float* in_re, const float* in_im, 
     if (rc) return rc;
     RowArgs a{in_re, in_im, out, nullptr, batch, n / 2 + 1, n, (float)(1.0 / (double)n)};
     e = launch_rows_c2r(plan->logn - 1, a, st);
+  } else if (plan->algorithm == TRNFFT_ALG_MIXED) {
+    int rc = check_ptrs("exec_c2r", {in_re, in_im, out}, 4);
+    if (rc) return rc;
+    MixedArgs a;
+    std::memset(&a, 0, sizeof a);
+    a.xr = in_re; a.xi = in_im; a.yr = out;
+    a.batch = batch; a.n = (int)n; a.npass = plan->npass;
+    a.codes = plan->codes;
+    a.tw = plan->twn;
+    a.scale = (float)(1.0 / (double)n);
+    e = launch_mixed(2, true, a, st);
   } else if (plan->algorithm == TRNFFT_ALG_BLUESTEIN && plan->H) {
     int rc = check_ptrs("exec_c2r", {in_re, in_im, out}, 4);
     if (rc) return rc;

@@ -37,6 +37,26 @@ struct BlueArgs {
 
 cudaError_t launch_bluestein(int logm, int mode, bool inv, const BlueArgs& a, cudaStream_t st);
 
+// Direct mixed-radix transforms of 7-smooth n <= 8192 (mixed.cu); modes as
+// BlueArgs.  Pass p's radix has code (codes >> 3p) & 7 (0..6 = 2, 3, 4, 5, 7,
+// 8, 16); tw holds, pass after pass, W_{ns R}^{k r} at k*(R-1) + r-1 for
+// k < ns (ns = product of the earlier radices), 1 <= r < R.
+struct MixedArgs {
+  const float* xr;
+  const float* xi;
+  float* yr;
+  float* yi;
+  long long batch;
+  int n;
+  int npass;
+  unsigned long long codes;
+  const float2* tw;
+  float scale;
+  int pitch;  // set by the launcher
+};
+
+cudaError_t launch_mixed(int mode, bool inv, const MixedArgs& a, cudaStream_t st);
+
 // Column-tile FFT pass (colpass.cu).  Tile = CT neighbouring columns
 // c in [c0, c0+CT) of L-point transforms, for outer block (o1, o2, o3).
 // Point j of column c is read at

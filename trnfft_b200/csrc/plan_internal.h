@@ -22,6 +22,11 @@ struct trnfft_plan_s {
   struct trnfft_plan_s* sub = nullptr;
   float* Hr = nullptr;
   float* Hi = nullptr;
+  // mixed radix (TRNFFT_ALG_MIXED): pass radices and W_n^i, i < n
+  int npass = 0;
+  int radix[16] = {0};
+  unsigned long long codes = 0;  // 3 bits per pass, see MixedArgs
+  float2* twn = nullptr;
   // double precision (trnfft_plan_enable_f64): power of two n > 4096: two-level
   // table of W_n; Bluestein: chirp and H = FFT_m(h)/m in double, and an m-point
   // sub-plan (also fp64-enabled) for the padded transforms
