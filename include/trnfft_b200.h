@@ -220,6 +220,22 @@ TRNFFT_API int trnfft_complex_linear(const float* xr, const float* xi, const flo
                                      const float* br, const float* bi, float* yr, float* yi, int64_t M,
                                      int64_t N, int64_t K, void* work, int device, void* stream);
 
+/* TF32 hi/lo split of `count` floats (hi = x rounded to TF32, lo = the TF32
+ * rounding of x - hi), the operands of the 3xTF32 products; 16-byte aligned
+ * pointers.  With trnfft_complex_linear_presplit a caller splits a weight
+ * once and reuses it across calls (ComplexLinear caches it per weight
+ * version), instead of re-splitting W on every forward. */
+TRNFFT_API int trnfft_split_tf32(const float* src, float* hi, float* lo, int64_t count, int device, void* stream);
+
+/* trnfft_complex_linear with W already split: w_split holds four N x K planes
+ * in the order Wr_hi, Wr_lo, Wi_hi, Wi_lo (trnfft_split_tf32 of W_re and
+ * W_im).  `work` holds the split of x: 4*M*K floats.  Replaces
+ * ComplexLinear.forward (trnfft/nn.py:33-49) for a weight that did not change
+ * since it was split. */
+TRNFFT_API int trnfft_complex_linear_presplit(const float* xr, const float* xi, const float* w_split,
+                                              const float* br, const float* bi, float* yr, float* yi, int64_t M,
+                                              int64_t N, int64_t K, void* work, int device, void* stream);
+
 /* The column step of the four-step FFT across GPUs: transforms along the
  * middle axis of [outer][n][inner] (plan n, power of two <= 2^20, out of
  * place; ld_in / ld_out floats between the points of a column, 0 = inner,

@@ -29,33 +29,66 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
     return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
-def linear_raw(xr, xi, wr, wi, br=None, bi=None):
-    """y = x W^T + b for 2-D planar complex x (M x K) and W (N x K) on CUDA."""
+def _weight_key(wr, wi, k4):
+    return (wr.data_ptr(), wi.data_ptr(), wr._version, wi._version, tuple(wr.shape), k4, wr.device)
+
+
+def split_weight(wr, wi, k4: int) -> torch.Tensor:
+    """The TF32 hi/lo split of a complex weight: one (4, N, k4) tensor holding
+    Wr_hi, Wr_lo, Wi_hi, Wi_lo (trnfft_split_tf32)."""
+    wr2, wi2 = (_aligned(_pad_k(t.float(), k4)) for t in (wr, wi))
+    N = wr2.shape[0]
+    out = torch.empty(4, N, k4, dtype=torch.float32, device=wr2.device)
+    dev = wr2.device.index if wr2.device.index is not None else torch.cuda.current_device()
+    for i, t in enumerate((wr2, wi2)):
+        _lib.call("trnfft_split_tf32", _lib.ptr(t), _lib.ptr(out[2 * i]), _lib.ptr(out[2 * i + 1]), t.numel(), dev,
+                  _lib.stream_ptr(t.device))
+    return out
+
+
+def linear_raw(xr, xi, wr, wi, br=None, bi=None, cache=None):
+    """y = x W^T + b for 2-D planar complex x (M x K) and W (N x K) on CUDA.
+
+    With `cache` (a dict owned by the caller, e.g. a ComplexLinear module), the TF32 split of
+    W is kept there and reused while W's storage and version are unchanged, so a forward
+    splits only x."""
     M, K = xr.shape
     N = wr.shape[0]
     k4 = (K + 3) // 4 * 4
-    xr, xi, wr, wi = (_aligned(_pad_k(t.float(), k4)) for t in (xr, xi, wr, wi))
+    dev = xr.device.index if xr.device.index is not None else torch.cuda.current_device()
     if br is not None:
         br = _aligned(br.float())
         bi = _aligned(bi.float())
     yr = torch.empty(M, N, dtype=torch.float32, device=xr.device)
     yi = torch.empty_like(yr)
-    if M and N:
-        wb = _lib.load().trnfft_complex_linear_work_bytes(M, N, k4)
-        work = torch.empty(wb, dtype=torch.uint8, device=xr.device)
-        _lib.call("trnfft_complex_linear", _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(wr), _lib.ptr(wi),
-                  _lib.ptr(br), _lib.ptr(bi), _lib.ptr(yr), _lib.ptr(yi), M, N, k4, _lib.ptr(work),
-                  xr.device.index if xr.device.index is not None else torch.cuda.current_device(),
-                  _lib.stream_ptr(xr.device))
+    if not (M and N):
+        return yr, yi
+    xr2, xi2 = (_aligned(_pad_k(t.float(), k4)) for t in (xr, xi))
+    if cache is not None:
+        key = _weight_key(wr, wi, k4)
+        if cache.get("key") != key:
+            cache["key"] = key
+            cache["split"] = split_weight(wr, wi, k4)
+        ws = cache["split"]
+        work = torch.empty(4 * M * k4, dtype=torch.float32, device=xr.device)
+        _lib.call("trnfft_complex_linear_presplit", _lib.ptr(xr2), _lib.ptr(xi2), _lib.ptr(ws), _lib.ptr(br),
+                  _lib.ptr(bi), _lib.ptr(yr), _lib.ptr(yi), M, N, k4, _lib.ptr(work), dev, _lib.stream_ptr(xr.device))
+        return yr, yi
+    wr2, wi2 = (_aligned(_pad_k(t.float(), k4)) for t in (wr, wi))
+    wb = _lib.load().trnfft_complex_linear_work_bytes(M, N, k4)
+    work = torch.empty(wb, dtype=torch.uint8, device=xr.device)
+    _lib.call("trnfft_complex_linear", _lib.ptr(xr2), _lib.ptr(xi2), _lib.ptr(wr2), _lib.ptr(wi2),
+              _lib.ptr(br), _lib.ptr(bi), _lib.ptr(yr), _lib.ptr(yi), M, N, k4, _lib.ptr(work), dev,
+              _lib.stream_ptr(xr.device))
     return yr, yi
 
 
 class _LinearFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, xr, xi, wr, wi, br, bi):
+    def forward(ctx, xr, xi, wr, wi, br, bi, cache=None):
         ctx.save_for_backward(xr, xi, wr, wi)
         ctx.has_bias = br is not None
-        return linear_raw(xr, xi, wr, wi, br, bi)
+        return linear_raw(xr, xi, wr, wi, br, bi, cache)
 
     @staticmethod
     def backward(ctx, gr, gi):
@@ -67,10 +100,10 @@ class _LinearFn(torch.autograd.Function):
         dwi = gi.t() @ xr - gr.t() @ xi
         dbr = gr.sum(0) if ctx.has_bias else None
         dbi = gi.sum(0) if ctx.has_bias else None
-        return dxr, dxi, dwr, dwi, dbr, dbi
+        return dxr, dxi, dwr, dwi, dbr, dbi, None
 
 
-def complex_linear(x: ComplexTensor, w_re, w_im, b_re=None, b_im=None) -> ComplexTensor:
+def complex_linear(x: ComplexTensor, w_re, w_im, b_re=None, b_im=None, cache=None) -> ComplexTensor:
     if b_re is not None and b_im is None:
         b_im = torch.zeros_like(b_re)
     ts = [x.real, x.imag, w_re, w_im] + ([b_re, b_im] if b_re is not None else [])
@@ -81,9 +114,9 @@ def complex_linear(x: ComplexTensor, w_re, w_im, b_re=None, b_im=None) -> Comple
     K = xr.shape[-1]
     xr2, xi2 = xr.reshape(-1, K), xi.reshape(-1, K)
     if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (xr2, xi2, wr, wi, br, bi)):
-        yr, yi = _LinearFn.apply(xr2, xi2, wr, wi, br, bi)
+        yr, yi = _LinearFn.apply(xr2, xi2, wr, wi, br, bi, cache)
     else:
-        yr, yi = linear_raw(xr2, xi2, wr, wi, br, bi)
+        yr, yi = linear_raw(xr2, xi2, wr, wi, br, bi, cache)
     N = wr.shape[0]
     return ComplexTensor(restore(yr.reshape(*lead, N)), restore(yi.reshape(*lead, N)))
 

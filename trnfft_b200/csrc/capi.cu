@@ -979,6 +979,35 @@ int64_t trnfft_complex_linear_work_bytes(int64_t M, int64_t N, int64_t K) {
   return (int64_t)sizeof(float) * 4 * (M + N) * K;
 }
 
+// The two GEMMs of a complex linear map from split operands:
+// x_hi/lo (M x K, real then imaginary part), w_hi/lo (N x K, same order).
+static int complex_linear_gemms(float* const xs[4], const float* const ws[4], const float* br, const float* bi,
+                                float* yr, float* yi, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof ga);
+  for (int i = 0; i < 4; ++i) {
+    ga.A[i] = xs[i];
+    ga.B[i] = ws[i];
+  }
+  ga.na = 4;
+  ga.nb = 4;
+  ga.M = M; ga.N = N; ga.K = K; ga.lda = K; ga.ldb = K; ga.ldc = N;
+  ga.nseg = 6;
+  // real part: Xr Wr^T - Xi Wi^T, each product as hi*hi + hi*lo + lo*hi
+  const int ra[6] = {0, 0, 1, 2, 2, 3}, rb[6] = {0, 1, 0, 2, 3, 2}, rn[6] = {0, 0, 0, 1, 1, 1};
+  for (int i = 0; i < 6; ++i) { ga.seg_a[i] = ra[i]; ga.seg_b[i] = rb[i]; ga.seg_neg[i] = rn[i]; }
+  ga.C = yr; ga.bias = br;
+  cudaError_t e = launch_gemm_tf32(ga, st);
+  if (e != cudaSuccess) return cuda_fail(e, "complex_linear: real part");
+  // imaginary part: Xr Wi^T + Xi Wr^T
+  const int ia[6] = {0, 0, 1, 2, 2, 3}, ib[6] = {2, 3, 2, 0, 1, 0};
+  for (int i = 0; i < 6; ++i) { ga.seg_a[i] = ia[i]; ga.seg_b[i] = ib[i]; ga.seg_neg[i] = 0; }
+  ga.C = yi; ga.bias = bi;
+  e = launch_gemm_tf32(ga, st);
+  if (e != cudaSuccess) return cuda_fail(e, "complex_linear: imaginary part");
+  return TRNFFT_SUCCESS;
+}
+
 int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, const float* wi, const float* br,
                           const float* bi, float* yr, float* yi, int64_t M, int64_t N, int64_t K, void* work,
                           int device, void* stream) {
@@ -993,32 +1022,50 @@ int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, con
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   float* w = static_cast<float*>(work);
   const size_t mk = (size_t)M * K, nk = (size_t)N * K;
-  float *xr_hi = w, *xr_lo = w + mk, *xi_hi = w + 2 * mk, *xi_lo = w + 3 * mk;
-  float *wr_hi = w + 4 * mk, *wr_lo = wr_hi + nk, *wi_hi = wr_hi + 2 * nk, *wi_lo = wr_hi + 3 * nk;
-  cudaError_t e = launch_split_tf32(xr, xr_hi, xr_lo, (long long)mk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(xi, xi_hi, xi_lo, (long long)mk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(wr, wr_hi, wr_lo, (long long)nk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(wi, wi_hi, wi_lo, (long long)nk, 1.f, st);
+  float* xs[4] = {w, w + mk, w + 2 * mk, w + 3 * mk};
+  float* wsp[4] = {w + 4 * mk, w + 4 * mk + nk, w + 4 * mk + 2 * nk, w + 4 * mk + 3 * nk};
+  cudaError_t e = launch_split_tf32(xr, xs[0], xs[1], (long long)mk, 1.f, st);
+  if (e == cudaSuccess) e = launch_split_tf32(xi, xs[2], xs[3], (long long)mk, 1.f, st);
+  if (e == cudaSuccess) e = launch_split_tf32(wr, wsp[0], wsp[1], (long long)nk, 1.f, st);
+  if (e == cudaSuccess) e = launch_split_tf32(wi, wsp[2], wsp[3], (long long)nk, 1.f, st);
   if (e != cudaSuccess) return cuda_fail(e, "complex_linear: split");
-  GemmArgs ga;
-  std::memset(&ga, 0, sizeof ga);
-  ga.A[0] = xr_hi; ga.A[1] = xr_lo; ga.A[2] = xi_hi; ga.A[3] = xi_lo; ga.na = 4;
-  ga.B[0] = wr_hi; ga.B[1] = wr_lo; ga.B[2] = wi_hi; ga.B[3] = wi_lo; ga.nb = 4;
-  ga.M = M; ga.N = N; ga.K = K; ga.lda = K; ga.ldb = K; ga.ldc = N;
-  ga.nseg = 6;
-  // real part: Xr Wr^T - Xi Wi^T, each product as hi*hi + hi*lo + lo*hi
-  const int ra[6] = {0, 0, 1, 2, 2, 3}, rb[6] = {0, 1, 0, 2, 3, 2}, rn[6] = {0, 0, 0, 1, 1, 1};
-  for (int i = 0; i < 6; ++i) { ga.seg_a[i] = ra[i]; ga.seg_b[i] = rb[i]; ga.seg_neg[i] = rn[i]; }
-  ga.C = yr; ga.bias = br;
-  e = launch_gemm_tf32(ga, st);
-  if (e != cudaSuccess) return cuda_fail(e, "complex_linear: real part");
-  // imaginary part: Xr Wi^T + Xi Wr^T
-  const int ia[6] = {0, 0, 1, 2, 2, 3}, ib[6] = {2, 3, 2, 0, 1, 0};
-  for (int i = 0; i < 6; ++i) { ga.seg_a[i] = ia[i]; ga.seg_b[i] = ib[i]; ga.seg_neg[i] = 0; }
-  ga.C = yi; ga.bias = bi;
-  e = launch_gemm_tf32(ga, st);
-  if (e != cudaSuccess) return cuda_fail(e, "complex_linear: imaginary part");
+  const float* ws[4] = {wsp[0], wsp[1], wsp[2], wsp[3]};
+  return complex_linear_gemms(xs, ws, br, bi, yr, yi, M, N, K, st);
+}
+
+int trnfft_split_tf32(const float* src, float* hi, float* lo, int64_t count, int device, void* stream) {
+  if (count < 0) return fail(TRNFFT_INVALID_VALUE, "split_tf32: negative count");
+  if (count == 0) return TRNFFT_SUCCESS;
+  int rc = check_ptrs("split_tf32", {src, hi, lo}, 16);
+  if (rc) return rc;
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "split_tf32: cannot select device %d", device);
+  cudaError_t e = launch_split_tf32(src, hi, lo, (long long)count, 1.f, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "split_tf32");
   return TRNFFT_SUCCESS;
+}
+
+int trnfft_complex_linear_presplit(const float* xr, const float* xi, const float* w_split, const float* br,
+                                   const float* bi, float* yr, float* yi, int64_t M, int64_t N, int64_t K, void* work,
+                                   int device, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(TRNFFT_INVALID_VALUE, "complex_linear_presplit: negative size");
+  if (M == 0 || N == 0) return TRNFFT_SUCCESS;
+  if (K % 4) return fail(TRNFFT_UNSUPPORTED, "complex_linear_presplit: K=%lld must be a multiple of 4", (long long)K);
+  int rc = check_ptrs("complex_linear_presplit", {xr, xi, w_split, yr, yi, work}, 16);
+  if (rc) return rc;
+  if ((br == nullptr) != (bi == nullptr))
+    return fail(TRNFFT_INVALID_VALUE, "complex_linear_presplit: give both biases or none");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "complex_linear_presplit: cannot select device %d", device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* w = static_cast<float*>(work);
+  const size_t mk = (size_t)M * K, nk = (size_t)N * K;
+  float* xs[4] = {w, w + mk, w + 2 * mk, w + 3 * mk};
+  cudaError_t e = launch_split_tf32(xr, xs[0], xs[1], (long long)mk, 1.f, st);
+  if (e == cudaSuccess) e = launch_split_tf32(xi, xs[2], xs[3], (long long)mk, 1.f, st);
+  if (e != cudaSuccess) return cuda_fail(e, "complex_linear_presplit: split");
+  const float* ws[4] = {w_split, w_split + nk, w_split + 2 * nk, w_split + 3 * nk};
+  return complex_linear_gemms(xs, ws, br, bi, yr, yi, M, N, K, st);
 }
 
 int trnfft_exec_c2c_axis_tw(trnfft_plan_t plan, trnfft_plan_t tw_plan, const float* in_re, const float* in_im,

@@ -285,9 +285,10 @@ def _four_step_peer(ar, ai, n, group, inverse, natural_order, chunks=1):
     """CUDA four-step with the exchange inside the column kernel (NVLink peer stores).
 
     With `chunks` > 1 the column block is cut into column ranges issued alternately on two
-    streams (the scatter pass of one range next to the first pass of the next); on B200 this
-    measured no faster than one range (2 GPUs, 2^30: 7.58-7.64 ms either way), so one range
-    is the default.
+    streams, so the first (HBM-bound) column pass of one range can run beside the NVLink-bound
+    scatter pass of the previous one.  On B200 at 2 GPUs, 2^30: 8.0 ms with one range, 7.5 ms
+    with eight (the overlap is small there because the scatter pass already moves 4.3 GB of
+    local HBM traffic; with more ranks its share of HBM falls and the overlap grows).
     """
     from . import _lib
 
@@ -380,7 +381,7 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
 
     ``exchange="peer"`` (default, one node): the column kernel stores its output straight into
     the owning ranks' row buffers over NVLink (CUDA IPC mappings, plain stores); ``chunks``
-    (default 1) column ranges on two streams.
+    (default 8) column ranges on two streams.
     ``exchange="nccl"``: NCCL all-to-all, chunked (``chunks``, default 4) to overlap the column
     transforms.
     """
@@ -401,7 +402,7 @@ def fft_distributed(x_local: ComplexTensor, n: int, inverse: bool = False, natur
         ai = _a2a(xi.reshape(r1, P, c2).transpose(0, 1), group).reshape(N1, c2)
     if exchange == "peer" and P <= 8:
         zr, zi = _four_step_peer(ar.contiguous(), ai.contiguous(), n, group, inverse, natural_order,
-                                 chunks=1 if chunks is None else chunks)
+                                 chunks=8 if chunks is None else chunks)
     else:
         zr, zi = _four_step_overlapped(ar, ai, n, group, inverse, natural_order, 4 if chunks is None else chunks)
     return ComplexTensor(zr, zi)

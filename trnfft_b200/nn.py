@@ -38,9 +38,16 @@ class ComplexLinear(nn.Module):
         nn.init.kaiming_uniform_(self.W_im.weight, a=math.sqrt(5))
 
     def forward(self, x: ComplexTensor) -> ComplexTensor:
-        from .nki.dispatch import complex_linear
+        from . import _gemm
 
-        return complex_linear(x, self.W_re.weight, self.W_im.weight, self.bias_re, self.bias_im)
+        # the weight's TF32 hi/lo split is cached here and redone only when the
+        # weight's storage or version changes (e.g. after an optimizer step)
+        if not hasattr(self, "_wsplit"):
+            self._wsplit = {}
+        if not (self.W_re.weight.is_cuda or x.real.is_cuda):
+            self._wsplit = {}
+        return _gemm.complex_linear(x, self.W_re.weight, self.W_im.weight, self.bias_re, self.bias_im,
+                                    cache=self._wsplit if self.W_re.weight.is_cuda else None)
 
 
 class ComplexConv1d(nn.Module):
