@@ -635,6 +635,143 @@ class SmallNGemm(SmallN):
         self.tensor_flops = sum(3 * 8.0 * self.batch * n * n for n in (256,))
 
 
+class Istft(Workload):
+    """Inverse of BASELINE configs[2]: istft of the 256 x 257 x 626 spectrogram back to 256 x 160000
+    samples (n_fft 512, hop 256, periodic Hann, centred), one fused kernel."""
+
+    metric = "iSTFT frames/s (256 x 626 frames, n_fft 512, hop 256, onesided)"
+    unit = "frames/s"
+
+    def __init__(self):
+        self.B, self.L, self.nfft, self.hop = 256, 160000, 512, 256
+        self.frames = 1 + (self.L + 2 * (self.nfft // 2) - self.nfft) // self.hop
+        self.name = "iSTFT 256 x 626 frames -> 160000 samples, n_fft=512, hop=256, periodic Hann (configs[2] inverse)"
+        self.work = float(self.B * self.frames)
+        bins = self.nfft // 2 + 1
+        self.dom_bytes = 8.0 * self.B * bins * self.frames + 4.0 * self.B * self.L
+        self.dominant = "fused iSTFT kernel (n_fft=512)"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+
+        self.win = torch.hann_window(self.nfft, device=dev)
+        x = torch.randn(self.B, self.L, device=dev, generator=g)
+        self.x = x
+        S = trnfft.stft(x, self.nfft, self.hop, window=self.win)
+        self.sr, self.si = S.real.contiguous(), S.imag.contiguous()
+        from trnfft_b200 import ComplexTensor
+
+        self.step = lambda: trnfft.istft(ComplexTensor(self.sr, self.si), self.nfft, self.hop, window=self.win,
+                                         length=self.L)
+        self.launches = {"istft": self.step}
+        self.launches_per_step = 1
+        self.inputs = [self.sr, self.si]
+        self.e2e_fn = lambda ts: [trnfft.istft(ComplexTensor(ts[0], ts[1]), self.nfft, self.hop, window=self.win,
+                                               length=self.L)]
+
+    def check(self, out):
+        return rel_err(out, self.x)
+
+    def ref_full_units(self):
+        return self.B
+
+    def ref_sample(self, T, units):
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(units, self.L, generator=g)
+        win = torch.hann_window(self.nfft)
+        S = T.stft(x, self.nfft, self.hop, window=win)
+        return ((lambda: T.istft(S, self.nfft, self.hop, window=win, length=self.L)), float(units * self.frames),
+                f"{units} of {self.B} spectrograms")
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        rng = np.random.default_rng(0)
+        w = rng.standard_normal((max(1, rows // 64), self.L)).astype(np.float32)
+        sr, si = O.stft(w, self.nfft, self.hop)
+        t0 = time.perf_counter()
+        O.istft(sr, si, self.nfft, self.hop, length=self.L)
+        return time.perf_counter() - t0, float(w.shape[0] * self.frames)
+
+
+class MaskApply(Workload):
+    """complex_mask_apply on the configs[2] spectrogram shape (256 x 257 x 626), one fused kernel
+    (the mask step between STFT and iSTFT)."""
+
+    metric = "complex mask apply, complex elements/s (256 x 257 x 626)"
+    unit = "elements/s"
+
+    def __init__(self):
+        self.shape = (256, 257, 626)
+        self.count = 256 * 257 * 626
+        self.name = "complex_mask_apply, mask and spectrogram 256 x 257 x 626 planar fp32 (configs[2] shape)"
+        self.work = float(self.count)
+        self.dom_bytes = 24.0 * self.count
+        self.dominant = "fused complex multiply kernel (float4)"
+
+    def setup(self, dev, g):
+        from trnfft_b200 import ComplexTensor
+        from trnfft_b200.nki.dispatch import complex_mask_apply
+
+        self.m = ComplexTensor(torch.randn(*self.shape, device=dev, generator=g),
+                               torch.randn(*self.shape, device=dev, generator=g))
+        self.s = ComplexTensor(torch.randn(*self.shape, device=dev, generator=g),
+                               torch.randn(*self.shape, device=dev, generator=g))
+        self.step = lambda: complex_mask_apply(self.m, self.s)
+        self.launches = {"mask": self.step}
+        self.launches_per_step = 1
+        self.inputs = [self.m.real, self.m.imag, self.s.real, self.s.imag]
+        self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(
+            complex_mask_apply(ComplexTensor(ts[0], ts[1]), ComplexTensor(ts[2], ts[3])))
+
+    def check(self, out):
+        want = torch.complex(self.m.real, self.m.imag) * torch.complex(self.s.real, self.s.imag)
+        return rel_err(torch.complex(out.real, out.imag), want)
+
+    def ref_full_units(self):
+        return self.shape[0]
+
+    def ref_sample(self, T, units):
+        from trnfft.nki.dispatch import complex_mask_apply as ref_mask
+
+        g = torch.Generator().manual_seed(0)
+        sh = (units,) + self.shape[1:]
+        m = T.ComplexTensor(torch.randn(*sh, generator=g), torch.randn(*sh, generator=g))
+        sp = T.ComplexTensor(torch.randn(*sh, generator=g), torch.randn(*sh, generator=g))
+        return (lambda: ref_mask(m, sp)), float(units * self.shape[1] * self.shape[2]), f"{units} of {self.shape[0]} rows"
+
+    def cpu_sample(self, threads, rows):
+        rng = np.random.default_rng(0)
+        r = max(1, rows // 16)
+        sh = (r,) + self.shape[1:]
+        a, b, c, d = (rng.standard_normal(sh).astype(np.float32) for _ in range(4))
+        t0 = time.perf_counter()
+        _ = (a * c - b * d, a * d + b * c)
+        return time.perf_counter() - t0, float(np.prod(sh))
+
+
+class C2CDouble(C2CRoundTrip):
+    """precision="double": the fp64 kernels on a float32 batch (widened and rounded back on the
+    device), fft + ifft round trip."""
+
+    dtype = "f64"
+
+    def __init__(self, n, batch, tag):
+        super().__init__(n, batch, tag)
+        self.name = f"batched C2C FFT+IFFT round trip in precision='double' (fp64 kernels), N={n}, batch={batch} ({tag})"
+        self.dominant = f"fp64 C2C kernels, N={n}"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+
+        trnfft.set_precision("double")
+        super().setup(dev, g)
+
+    def ref_sample(self, T, units):
+        T.set_precision("double")
+        return super().ref_sample(T, units)
+
+
 WORKLOADS = {
     "linear": LinearWL,
     "smalln_gemm": SmallNGemm,
@@ -646,6 +783,10 @@ WORKLOADS = {
     "bluestein6000": lambda: C2CRoundTrip(6000, 4096, "BASELINE configs[3]"),
     "large": Large,
     "fft2": Fft2,
+    "istft": Istft,
+    "mask": MaskApply,
+    "double4093": lambda: C2CDouble(4093, 4096, "BASELINE configs[3], precision double"),
+    "double1024": lambda: C2CDouble(1024, 8192, "BASELINE configs[0], precision double"),
 }
 
 
@@ -944,7 +1085,8 @@ def run_ours(args, world, rank, local):
     out = {
         "metric": wl.metric, "value": round(scale_value(value, wl.unit), 3), "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
+        "dtype": getattr(wl, "dtype", "f32"),
         "data": "synthetic",
         "config": {"workload": wl.name,
                    "parallelism": ("1 GPU" if world == 1 else

@@ -188,7 +188,8 @@ TRNFFT_API int trnfft_exec_stft(trnfft_plan_t plan, const float* signal, int64_t
  * 1/sqrt(n_fft).  `out` receives batch rows of out_len samples starting at
  * overlap-add position n_fft/2 when `center` (else 0), zero past
  * n_fft + (frames-1)*hop; the caller derives out_len from `length` as
- * api.py:454-468 does.  One kernel, one pass over the spectrum. */
+ * api.py:454-468 does.  One kernel, one pass over the spectrum.  hop up to
+ * 8192 samples and signals below 2^31 samples (else TRNFFT_UNSUPPORTED). */
 TRNFFT_API int trnfft_exec_istft(trnfft_plan_t plan, const float* in_re, const float* in_im, int64_t batch,
                                  int64_t frames, int64_t hop, const float* window, int center, int normalized,
                                  int onesided, int64_t out_len, float* out, void* stream);

@@ -466,7 +466,8 @@ def istft(sr: torch.Tensor, si: torch.Tensor, n_fft: int, hop: int, w: torch.Ten
     Power-of-two n_fft up to 8192 without autograd runs the fused kernel
     (trnfft_exec_istft); other cases compose the library's inverse transforms with a
     device overlap-add."""
-    fused = (4 <= n_fft <= 8192 and (n_fft & (n_fft - 1)) == 0 and not _needs_grad(sr, si, w)
+    fused = (4 <= n_fft <= 8192 and (n_fft & (n_fft - 1)) == 0 and 1 <= hop <= 8192
+             and not _needs_grad(sr, si, w) and sr.dtype == torch.float32
              and sr.shape[-2] == (n_fft // 2 + 1 if onesided else n_fft))
     if not fused:
         return _istft_composite(sr, si, n_fft, hop, w, center, normalized, onesided, length)

@@ -1301,6 +1301,9 @@ int trnfft_exec_istft(trnfft_plan_t plan, const float* in_re, const float* in_im
   a.pad_front = center ? n / 2 : 0;
   a.exp_len = n + (frames - 1) * hop;
   a.total = a.exp_len > a.pad_front + out_len ? a.exp_len : a.pad_front + out_len;
+  if (a.total >= (1LL << 31) - 16384)
+    return fail(TRNFFT_UNSUPPORTED, "exec_istft: signals of 2^31 samples or more are not supported");
+  if (hop > 8192) return fail(TRNFFT_UNSUPPORTED, "exec_istft: hop %lld above 8192 samples", (long long)hop);
   a.onesided = onesided ? 1 : 0;
   a.scale = (float)((normalized ? std::sqrt((double)n) : 1.0) / (double)n);
   cudaError_t e = launch_istft(plan->logn, a, reinterpret_cast<cudaStream_t>(stream));

@@ -9,17 +9,20 @@
 // (api.py:450-452); finally the centre padding is cut and the result trimmed
 // or zero-padded to `length` (api.py:454-468).
 //
-// Here one kernel does all of it.  A block owns one segment of SEG output
-// samples of one signal.  It walks over the frames that touch the segment in
-// chunks of G frames: it stages the chunk's spectrum columns ([bins][G], the
-// G frames are contiguous in the (freq, time) layout, so every load is a run
-// of G floats), runs G real inverse transforms on chip (an n_fft/2-point
-// complex FFT of Z_k = E_k + i O_k, the same packing as the forward real
-// kernels), and adds each frame's samples, windowed and raw, into two
-// segment accumulators in shared memory.  The envelope sum_f w[t - f hop]^2 is
-// evaluated per sample from the window, and every output sample is written
-// exactly once.  Frames shared by two neighbouring segments are transformed by
-// both blocks (a few percent extra arithmetic, no extra writes).
+// Here one kernel does all of it.  A block owns the samples of P consecutive
+// frame starts of one signal (a segment of P * hop samples) and transforms
+// the P + H frames that touch it (H = ceil(n_fft / hop) - 1 earlier frames
+// reach into the segment), in chunks of G frames: it stages the chunk's
+// spectrum columns ([bins][G]; the G frames are contiguous in the (freq, time)
+// layout, so every load is a run of G floats), runs G real inverse transforms
+// on chip (an n_fft/2-point complex FFT of Z_k = E_k + i O_k, the packing of
+// the forward real kernels), and adds each frame's samples - windowed, raw,
+// and the squared window - into three segment accumulators in shared memory.
+// Each thread owns a fixed residue class of the segment's samples, so frames
+// add into a sample in frame order, like the reference's loop, without
+// atomics.  Every output sample is written exactly once; the H frames shared
+// with the previous segment are transformed twice (for n_fft = 2 hop, one in
+// G = 8).
 #include "fft_common.cuh"
 #include "kernels.h"
 
@@ -34,13 +37,25 @@ struct IstftGeom {
   static constexpr int THREADS = G * S::T;  // every thread owns a slice of one frame
   static constexpr int M = S::N;
   static constexpr int FP = S::NP + ((2 - S::NP % 16) + 16) % 16;  // frame pitch (float2)
-  // frames (float2) + spectrum tile (2 planes of (M+1) x G floats); the segment
-  // accumulators (2 x SEG floats) follow, sized at launch
-  static constexpr size_t fixed_smem = (size_t)G * FP * sizeof(float2) + 2 * (size_t)(M + 1) * G * sizeof(float);
+  // the spectrum tile (2 planes of (M+1) x G floats) shares its space with the frames
+  // (float2): it is read into registers before the first pass writes the frames
+  static constexpr int TP = G + 1;  // tile floats per bin: an odd pitch keeps the C2R loads conflict-free
+  static constexpr size_t tile_bytes = 2 * (size_t)(M + 1) * TP * sizeof(float);
+  static constexpr size_t frame_bytes = (size_t)G * FP * sizeof(float2);
+  // ... followed by the segment accumulators (3 x SEG floats), sized at launch
+  static constexpr size_t fixed_smem = ((tile_bytes > frame_bytes ? tile_bytes : frame_bytes) + 15) / 16 * 16;
+  static constexpr int MINB = 5;
 };
 
+// 4-byte asynchronous global -> shared copy; src_bytes = 0 fills zero
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem, int src_bytes) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 template <int LOGM>
-__global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS) k_istft(IstftArgs a) {
+__global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS, IstftGeom<LOGM>::MINB) k_istft(IstftArgs a) {
   using GM = IstftGeom<LOGM>;
   using S = typename GM::S;
   constexpr int M = S::N;
@@ -49,19 +64,21 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS) k_istft(IstftArgs a)
   constexpr int G = GM::G;
   extern __shared__ float2 sm2[];
   float2* frames = sm2;
-  float* tre = reinterpret_cast<float*>(sm2 + G * GM::FP);
-  float* tim = tre + (M + 1) * G;
-  float* acc_w = tim + (M + 1) * G;
-  float* acc_r = acc_w + a.seg;
+  float* tre = reinterpret_cast<float*>(sm2);  // aliases the frames (see IstftGeom)
+  float* tim = tre + (M + 1) * GM::TP;
+  float* acc_w = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(sm2) + GM::fixed_smem);
+  float* acc_r = acc_w + a.seg;      // unwindowed overlap-add
+  float* acc_e = acc_r + a.seg;      // envelope sum_f w[t - f hop]^2
 
   const long long b = blockIdx.x / a.nseg;
-  const long long t0 = (long long)(blockIdx.x % a.nseg) * a.seg;
-  const long long t1 = min(t0 + a.seg, a.total);
+  // 32-bit sample indices within one signal (the host rejects signals of 2^31 samples)
+  const int t0 = (int)((blockIdx.x % a.nseg) * (long long)a.seg);
+  const int t1 = (int)min((long long)t0 + a.seg, a.total);
   const int tid = threadIdx.x;
   const int g = tid / S::T;
   const int j = tid % S::T;
-  const long long hop = a.hop;
-  const long long F = a.frames;
+  const int hop = (int)a.hop;
+  const int F = (int)a.frames;
   const int nbins = a.onesided ? M + 1 : N;
   const float* __restrict__ xr = a.xr + b * (long long)nbins * F;
   const float* __restrict__ xi = a.xi + b * (long long)nbins * F;
@@ -70,31 +87,43 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS) k_istft(IstftArgs a)
   for (int i = tid; i < a.seg; i += GM::THREADS) {
     acc_w[i] = 0.f;
     acc_r[i] = 0.f;
+    acc_e[i] = 0.f;
   }
   // frames f with [f hop, f hop + N) meeting [t0, t1)
-  long long flo = t0 - N + 1 <= 0 ? 0 : (t0 - N + 1 + hop - 1) / hop;
-  long long fhi = (t1 - 1) / hop;
+  const int flo = t0 - N + 1 <= 0 ? 0 : (t0 - N + hop) / hop;
+  int fhi = (t1 - 1) / hop;
   if (fhi > F - 1) fhi = F - 1;
 
-  for (long long fc = flo; fc <= fhi; fc += G) {
-    // stage the chunk's spectrum: tile[k][gg], k in [0, M]
-    for (int idx = tid; idx < (M + 1) * G; idx += GM::THREADS) {
-      const int gg = idx % G;
-      const int k = idx / G;
-      const long long f = fc + gg;
-      float r = 0.f, m = 0.f;
-      if (f <= fhi) {
-        r = __ldg(xr + (long long)k * F + f);
-        m = __ldg(xi + (long long)k * F + f);
-        if (!a.onesided) {
+  for (int fc = flo; fc <= fhi; fc += G) {
+    // stage the chunk's spectrum: tile[k][gg], k in [0, M]; the G frames of a bin are
+    // contiguous in memory.  One-sided spectra go through asynchronous 4-byte copies, all in
+    // flight at once (frames past the last one are zero-filled).
+    if (a.onesided) {
+      for (int idx = tid; idx < (M + 1) * G; idx += GM::THREADS) {
+        const int gg = idx % G;
+        const int k = idx / G;
+        const int f = fc + gg;
+        const bool in = f <= fhi;
+        const long long off = in ? (long long)k * F + f : 0;
+        cp_async4(tre + k * GM::TP + gg, xr + off, in ? 4 : 0);
+        cp_async4(tim + k * GM::TP + gg, xi + off, in ? 4 : 0);
+      }
+      cp_async_wait_all();
+    } else {
+      for (int idx = tid; idx < (M + 1) * G; idx += GM::THREADS) {
+        const int gg = idx % G;
+        const int k = idx / G;
+        const int f = fc + gg;
+        float r = 0.f, m = 0.f;
+        if (f <= fhi) {
           // real part of the full inverse transform = C2R of (X_k + conj X_{N-k}) / 2
           const int km = (N - k) & (N - 1);
-          r = 0.5f * (r + __ldg(xr + (long long)km * F + f));
-          m = 0.5f * (m - __ldg(xi + (long long)km * F + f));
+          r = 0.5f * (__ldg(xr + (long long)k * F + f) + __ldg(xr + (long long)km * F + f));
+          m = 0.5f * (__ldg(xi + (long long)k * F + f) - __ldg(xi + (long long)km * F + f));
         }
+        tre[k * GM::TP + gg] = r;
+        tim[k * GM::TP + gg] = m;
       }
-      tre[idx] = r;
-      tim[idx] = m;
     }
     __syncthreads();
     {
@@ -103,8 +132,8 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS) k_istft(IstftArgs a)
       // 2 Z_k = (X_k + conj X_{M-k}) + i (X_k - conj X_{M-k}) conj(W_N^k)
       pass_load<LOGM, GM::LE, 0>(j, vr, vi, [&](int k, float& r, float& m) {
         const int km = M - k;
-        const float ar = tre[k * G + g], ai = (k == 0) ? 0.f : tim[k * G + g];
-        const float br = tre[km * G + g], bi = (km == M) ? 0.f : tim[km * G + g];
+        const float ar = tre[k * GM::TP + g], ai = (k == 0) ? 0.f : tim[k * GM::TP + g];
+        const float br = tre[km * GM::TP + g], bi = (km == M) ? 0.f : tim[km * GM::TP + g];
         const float er = ar + br, ei = ai - bi;
         const float dr = ar - br, di = ai + bi;
         const float2 tw = tw_lookup(k << (kTwLog - LOGN));
@@ -113,45 +142,45 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS) k_istft(IstftArgs a)
         r = er - oi;
         m = ei + orr;
       });
+      __syncthreads();  // the tile is read: the frames may overwrite it
       pass_compute_store<LOGM, GM::LE, 0, true>(j, vr, vi, [&](int i, float r, float m) {
         sb[spad<S::SH>(i)] = make_float2(r, m);
       });
     }
     __syncthreads();
     smem_passes<LOGM, GM::LE, true, 1, S::P>(j, frames + g * GM::FP);
-    // overlap-add of the chunk into the segment
-    const long long fend = min(fc + G - 1, fhi);
-    for (long long t = t0 + tid; t < t1; t += GM::THREADS) {
-      float sw = 0.f, sr = 0.f;
-      for (long long f = fc; f <= fend; ++f) {
-        const long long off = t - f * hop;
-        if (off < 0 || off >= N) continue;
-        const float2 z = frames[(int)(f - fc) * GM::FP + spad<S::SH>((int)(off >> 1))];
+    // overlap-add, frame by frame.  Thread tid owns the samples t = t0 + tid (mod THREADS),
+    // so the frames of the chunk add into each sample in frame order (as the reference's
+    // loop does) with no two threads touching one sample.
+    const int fe = fc + G - 1 < fhi ? fc + G - 1 : fhi;
+    for (int f = fc; f <= fe; ++f) {
+      const int fs = f * hop;
+      const int lo = fs > t0 ? fs : t0;
+      const int hi = fs + N < t1 ? fs + N : t1;
+      // first owned sample >= lo
+      int t = lo + ((t0 + tid - lo) % GM::THREADS + GM::THREADS) % GM::THREADS;
+      const float2* fr = frames + (f - fc) * GM::FP;
+      for (; t < hi; t += GM::THREADS) {
+        const int off = t - fs;
+        const float2 z = fr[spad<S::SH>(off >> 1)];
         const float v = ((off & 1) ? z.y : z.x) * a.scale;
-        sw = fmaf(v, __ldg(w + off), sw);
-        sr += v;
+        const float ww = __ldg(w + off);
+        acc_w[t - t0] = fmaf(v, ww, acc_w[t - t0]);
+        acc_r[t - t0] += v;
+        acc_e[t - t0] = fmaf(ww, ww, acc_e[t - t0]);
       }
-      acc_w[t - t0] += sw;
-      acc_r[t - t0] += sr;
     }
     __syncthreads();
   }
 
-  // envelope, normalisation, centre trim and length
+  // normalisation, centre trim and length
   float* __restrict__ y = a.y + b * a.out_len;
-  for (long long t = t0 + tid; t < t1; t += GM::THREADS) {
-    const long long o = t - a.pad_front;
+  for (int t = t0 + tid; t < t1; t += GM::THREADS) {
+    const long long o = (long long)t - a.pad_front;
     if (o < 0 || o >= a.out_len) continue;
     float out = 0.f;
     if (t < a.exp_len) {
-      long long f0 = t - N + 1 <= 0 ? 0 : (t - N + 1 + hop - 1) / hop;
-      long long f1 = t / hop;
-      if (f1 > F - 1) f1 = F - 1;
-      float env = 0.f;
-      for (long long f = f0; f <= f1; ++f) {
-        const float ww = __ldg(w + (t - f * hop));
-        env = fmaf(ww, ww, env);
-      }
+      const float env = acc_e[t - t0];
       out = env > 1e-8f ? acc_w[t - t0] / env : acc_r[t - t0];
     }
     y[o] = out;
@@ -161,17 +190,23 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS) k_istft(IstftArgs a)
 template <int LOGM>
 static cudaError_t launch_istft_t(IstftArgs a, cudaStream_t st) {
   using GM = IstftGeom<LOGM>;
-  // segment: up to 4 chunks of G frames' worth of hops, about 4096 samples
-  long long seg = (long long)GM::G * a.hop;
-  long long cps = seg > 0 ? 4096 / seg : 1;
-  if (cps < 1) cps = 1;
-  if (cps > 4) cps = 4;
-  seg *= cps;
-  if (seg > 16384) seg = 16384;
-  if (seg < 1) seg = 1;
+  constexpr int N = 2 * GM::M;
+  // A block owns P consecutive frame starts (its segment is P * hop samples) and needs the
+  // H = ceil(N / hop) - 1 frames before them: P + H = K * G frames, K whole chunks.
+  const long long H = (N - 1) / a.hop;
+  long long K = (H + GM::G) / GM::G;  // smallest K with K * G > H
+  if (K < 1) K = 1;
+  long long P = K * GM::G - H;
+  long long seg = P * a.hop;
+  // keep the three segment accumulators within 96 KB
+  while (seg * 12 > 96 * 1024 && P > 1) {
+    --P;
+    seg = P * a.hop;
+  }
+  if (seg * 12 > 96 * 1024) return cudaErrorInvalidValue;  // hop beyond 8192 samples
   a.seg = (int)seg;
   a.nseg = (a.total + seg - 1) / seg;
-  const size_t smem = GM::fixed_smem + 2 * (size_t)seg * sizeof(float);
+  const size_t smem = GM::fixed_smem + 3 * (size_t)seg * sizeof(float);
   auto kern = k_istft<LOGM>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
