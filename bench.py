@@ -783,6 +783,8 @@ WORKLOADS = {
     "bluestein6000": lambda: C2CRoundTrip(6000, 4096, "BASELINE configs[3]"),
     "large": Large,
     "fft2": Fft2,
+    "rows8192": lambda: C2CRoundTrip(8192, 8192, "one-pass rows of 8192 points (k_c2c_big)"),
+    "rows16384": lambda: C2CRoundTrip(16384, 4096, "one-pass rows of 16384 points (k_c2c_big), the fft2 / four-step row pass"),
     "istft": Istft,
     "mask": MaskApply,
     "double4093": lambda: C2CDouble(4093, 4096, "BASELINE configs[3], precision double"),

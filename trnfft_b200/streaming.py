@@ -4,8 +4,11 @@ Batched transforms act on every row independently, so a batch that lives in
 host memory can stream through the GPU in row chunks: while chunk c is being
 transformed, chunk c+1 is copied in and chunk c-1 is copied out.  PCIe moves
 data both ways at once, so with the copies of neighbouring chunks on
-different CUDA streams the step costs about one direction's transfer time
-instead of the sum of upload, compute and download.
+different CUDA streams the step costs less than the sum of upload, compute
+and download.  Measured on the B200 hosts here (PCIe 5 x16): 55 GB/s up,
+53 GB/s down, 79 GB/s both ways at once; a 64 MiB-each-way fft+ifft batch
+streams in 1.94 ms with 4 chunks on 2 streams, against 1.70 ms for the bare
+two-way copy and 2.6 ms with unpipelined copies.
 
 ``map_rows(fn, host_inputs)`` runs ``fn`` (a function of device tensors that
 returns device tensors, such as ``lambda x: [trnfft.fft(x).real, ...]``) on
@@ -41,7 +44,7 @@ def _side_streams(device: torch.device, n: int):
     return s
 
 
-def map_rows(fn, host_inputs, nchunks: int = 8, nstreams: int = 3, device=None, host_outputs=None):
+def map_rows(fn, host_inputs, nchunks: int = 4, nstreams: int = 2, device=None, host_outputs=None):
     """Apply `fn` to row chunks of host tensors with copies overlapped on `nstreams` streams.
 
     host_inputs: CPU tensors sharing their leading dimension (pinned memory makes the copies
