@@ -281,6 +281,17 @@ TRNFFT_API int trnfft_exec_fourstep_scatter(trnfft_plan_t plan, trnfft_plan_t tw
                                             float* const* peer_im, int64_t rows_per_peer, int64_t peer_ld,
                                             int64_t peer_col0, void* work, void* stream);
 
+/* Strided block copy on `stream` (device `device` current): `height` rows of
+ * `width` bytes from src (rows spitch bytes apart) to dst (dpitch apart),
+ * either side local or a peer's buffer mapped with trnfft_ipc_open; the copy
+ * engines move it over NVLink.  The exchange step of fft2 across GPUs: each
+ * rank writes its column blocks straight into the owners' buffers, replacing
+ * the reference's transpose (trnfft/api.py:496-516) without a transposing
+ * kernel or an all-to-all staging copy.  No counterpart in the reference (its
+ * transforms run on one device). */
+TRNFFT_API int trnfft_copy2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width,
+                             int64_t height, int device, void* stream);
+
 /* Batched real-to-complex transform: rows of n reals -> rows of n/2+1 bins.
  * Replaces trnfft.rfft (trnfft/api.py:38-46), which runs a full complex
  * transform of the real row and keeps the first n//2+1 bins. */

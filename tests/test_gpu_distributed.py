@@ -55,6 +55,13 @@ def _worker(rank, world, port, q):
     g = D.fft2_distributed(ComplexTensor(torch.tensor(f.real[h0:h1].copy(), device="cuda"),
                                          torch.tensor(f.imag[h0:h1].copy(), device="cuda")))
     res["fft2"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
+    fl = ComplexTensor(torch.tensor(f.real[h0:h1].copy(), device="cuda"), torch.tensor(f.imag[h0:h1].copy(), device="cuda"))
+    g = D.fft2_distributed(fl, natural_order=False)  # column block [H][W/P] (peer copies)
+    res["fft2_cols"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
+    g = D.fft2_distributed(fl, exchange="nccl")
+    res["fft2_nccl"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
+    g = D.fft2_distributed(fl)  # second peer call reuses the mapped planes
+    res["fft2_2"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
     torch.cuda.synchronize()
     q.put((rank, res))
     dist.barrier()
@@ -95,4 +102,9 @@ def test_two_gpu_four_step_and_fft2():
     assert rel(cat("inv"), np.fft.ifft(x)) < 2e-6
     H, W = 2048, 4096
     f = (rng.standard_normal((H, W)) + 1j * rng.standard_normal((H, W))).astype(np.complex64).astype(np.complex128)
-    assert rel(cat("fft2"), np.fft.fft2(f)) < 2e-6
+    F = np.fft.fft2(f)
+    assert rel(cat("fft2"), F) < 2e-6
+    assert rel(cat("fft2_nccl"), F) < 2e-6
+    assert rel(cat("fft2_2"), F) < 2e-6
+    cols = np.concatenate([out[r]["fft2_cols"][0] + 1j * out[r]["fft2_cols"][1] for r in range(world)], axis=1)
+    assert rel(cols, F) < 2e-6

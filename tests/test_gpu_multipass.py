@@ -213,3 +213,19 @@ def test_fourstep_scatter_one_gpu(monkeypatch, n1, work_needed, inverse, cap):
     assert rel_l2(got[:, peer_col0:peer_col0 + cols], y) < 2e-6
     untouched = np.concatenate([got[:, :peer_col0], got[:, peer_col0 + cols:]], axis=1)
     assert not untouched.any()
+
+
+@pytest.mark.parametrize("n", [1 << 11, 1 << 17, 1 << 21, 3 * 4096])
+def test_stage_parallel_fft_vs_fp64(n):
+    """multi_core_fft's four-step (fused column twiddle for powers of two) against fp64."""
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal(n) + 1j * rng.standard_normal(n)).astype(np.complex64)
+    xc = ComplexTensor(cuda(x.real), cuda(x.imag))
+    multicore.set_multicore(True)
+    try:
+        y = multicore.multi_core_fft(xc)
+        z = multicore.multi_core_fft(xc, inverse=True)
+    finally:
+        multicore.set_multicore(False)
+    assert rel_l2(cplx(y), np.fft.fft(x.astype(np.complex128))) < TOL
+    assert rel_l2(cplx(z), np.fft.ifft(x.astype(np.complex128))) < TOL

@@ -58,6 +58,7 @@ SIGNATURES = {
     "trnfft_exec_fourstep_scatter": (_INT, [_P, _P, _P, _P, _I64, _I64, _INT, _I64, _INT,
                                             ctypes.POINTER(_P), ctypes.POINTER(_P), _I64, _I64, _I64, _P, _P]),
     "trnfft_exec_r2c": (_INT, [_P, _P, _P, _P, _I64, _P, _P]),
+    "trnfft_copy2d": (_INT, [_P, _I64, _P, _I64, _I64, _I64, _INT, _P]),
     "trnfft_plan_enable_f64": (_INT, [_P]),
     "trnfft_plan_query_f64": (_INT, [_P, _I64, ctypes.POINTER(_I64)]),
     "trnfft_exec_c2c_f64": (_INT, [_P, _P, _P, _P, _P, _I64, _INT, _P, _P]),

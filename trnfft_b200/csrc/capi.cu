@@ -1391,4 +1391,18 @@ int trnfft_convert_f32_f64(const void* src, void* dst, int64_t count, int to_dou
   return TRNFFT_SUCCESS;
 }
 
+int trnfft_copy2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                  int device, void* stream) {
+  if (dpitch < width || spitch < width || width < 0 || height < 0)
+    return fail(TRNFFT_INVALID_VALUE, "copy2d: bad pitch/width/height");
+  if (width == 0 || height == 0) return TRNFFT_SUCCESS;
+  if (!dst || !src) return fail(TRNFFT_INVALID_VALUE, "copy2d: null pointer");
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "copy2d: cannot select device %d", device);
+  cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dpitch, src, (size_t)spitch, (size_t)width, (size_t)height,
+                                    cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "copy2d");
+  return TRNFFT_SUCCESS;
+}
+
 }  // extern "C"

@@ -208,15 +208,18 @@ def _four_step_overlapped(ar, ai, n, group, inverse, natural_order, chunks):
 
 
 class _PeerExchange:
-    """Row buffers [N1/P][N2] on every rank, mapped into every other rank by CUDA IPC."""
+    """Two float planes on every rank (the four-step's row buffers [N1/P][N2], or `nfloats`
+    each), mapped into every other rank by CUDA IPC."""
 
-    def __init__(self, n, group, dev):
+    def __init__(self, n, group, dev, nfloats=None):
         from . import _lib
 
         P, p = _world(group)
-        N1, N2 = _split_n(n)
-        self.rows, self.cols = N1 // P, N2
-        nbytes = self.rows * self.cols * 4
+        if nfloats is None:
+            N1, N2 = _split_n(n)
+            self.rows, self.cols = N1 // P, N2
+            nfloats = self.rows * self.cols
+        nbytes = nfloats * 4
         lib = _lib.load()
         hb = lib.trnfft_ipc_handle_bytes()
         self.dev = dev
@@ -428,9 +431,76 @@ def _fft2_exchange(xr, xi, group, inverse, natural_order, row_fft, col_fft):
     return br.permute(1, 0, 2).reshape(hr, w).contiguous(), bi.permute(1, 0, 2).reshape(hr, w).contiguous()
 
 
+def _fft2_peer(xr, xi, group, inverse, natural_order):
+    """fft2 of row blocks [H/P][W] with the exchanges as 2-D peer copies (copy engines over NVLink).
+
+    Row transforms; every rank copies its column block q of its rows straight into rank q's
+    receive planes [H][W/P] (rows p*H/P ..), so after one barrier each rank holds full columns;
+    strided column transforms; for natural order the column results go back the same way into
+    [H/P][W] planes, then into the result tensor.  No transposing kernels, no staging copies.
+    """
+    from . import _lib, _ops
+
+    P, p = _world(group)
+    hr, w = xr.shape
+    h = hr * P
+    cw = w // P
+    dev = xr.device
+    key = ("fft2", hr, w, P, dev.index, id(group))
+    entry = _exchanges.get(key)
+    if entry is None or entry[0] is not group:
+        entry = _exchanges[key] = (group, _PeerExchange(0, group, dev, nfloats=h * cw),
+                                   _PeerExchange(0, group, dev, nfloats=hr * w) if natural_order else None)
+    cols_ex, back_ex = entry[1], entry[2]
+    if natural_order and back_ex is None:
+        back_ex = _PeerExchange(0, group, dev, nfloats=hr * w)
+        _exchanges[key] = (group, cols_ex, back_ex)
+    st = _lib.stream_ptr(dev)
+    di = dev.index
+    yr, yi = _ops.c2c_raw(xr, xi, inverse)  # rows, [hr][w]
+    _device_barrier(group, dev)  # every rank is done reading its receive planes
+    for q in range(P):
+        for src, dst in ((yr, cols_ex.peer_re[q]), (yi, cols_ex.peer_im[q])):
+            _lib.call("trnfft_copy2d", ctypes.c_void_p(dst + 4 * p * hr * cw), cw * 4,
+                      ctypes.c_void_p(src.data_ptr() + 4 * q * cw), w * 4, cw * 4, hr, di, st)
+    _device_barrier(group, dev)  # every block has landed
+    zr = torch.empty(h, cw, dtype=torch.float32, device=dev)
+    zi = torch.empty_like(zr)
+    plan = _lib.device_plan(h, dev)
+    _lib.call("trnfft_exec_c2c_axis", plan.handle, cols_ex.local[0], cols_ex.local[1], _lib.ptr(zr), _lib.ptr(zi),
+              1, cw, int(bool(inverse)), None, st)
+    if not natural_order:
+        return zr, zi
+    _device_barrier(group, dev)
+    for q in range(P):
+        for src, dst in ((zr, back_ex.peer_re[q]), (zi, back_ex.peer_im[q])):
+            _lib.call("trnfft_copy2d", ctypes.c_void_p(dst + 4 * p * cw), w * 4,
+                      ctypes.c_void_p(src.data_ptr() + 4 * q * hr * cw), cw * 4, cw * 4, hr, di, st)
+    _device_barrier(group, dev)
+    outr = torch.empty(hr, w, dtype=torch.float32, device=dev)
+    outi = torch.empty_like(outr)
+    for dst, src in ((outr, back_ex.local[0]), (outi, back_ex.local[1])):
+        _lib.call("trnfft_copy2d", _lib.ptr(dst), w * 4, src, w * 4, w * 4, hr, di, st)
+    return outr, outi
+
+
 def fft2_distributed(x_local: ComplexTensor, inverse: bool = False, natural_order: bool = True,
-                     group=None) -> ComplexTensor:
-    """fft2 of an [H][W] field whose rows are split evenly over the ranks ([H/P][W] each)."""
-    zr, zi = _fft2_exchange(x_local.real.float().contiguous(), x_local.imag.float().contiguous(), group,
-                            inverse, natural_order, _cuda_row_fft, _cuda_col_fft)
+                     group=None, exchange: str = "peer") -> ComplexTensor:
+    """fft2 of an [H][W] field whose rows are split evenly over the ranks ([H/P][W] each).
+
+    ``exchange="peer"`` (default on one node, up to 8 ranks, power-of-two H): 2-D peer copies into
+    CUDA-IPC-mapped planes (``_fft2_peer``); ``exchange="nccl"``: NCCL all-to-all with the
+    transposes around it.  The result is [H/P][W] rows (``natural_order``) or the column block
+    [H][W/P] of this rank."""
+    P, _ = _world(group)
+    xr = x_local.real.float().contiguous()
+    xi = x_local.imag.float().contiguous()
+    hr, w = xr.shape
+    h = hr * P
+    if w % P:
+        raise ValueError("fft2_distributed: the width must split evenly over the ranks")
+    if exchange == "peer" and P <= 8 and xr.is_cuda and h & (h - 1) == 0 and h <= (1 << 20):
+        zr, zi = _fft2_peer(xr, xi, group, inverse, natural_order)
+    else:
+        zr, zi = _fft2_exchange(xr, xi, group, inverse, natural_order, _cuda_row_fft, _cuda_col_fft)
     return ComplexTensor(zr, zi)

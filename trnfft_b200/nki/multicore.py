@@ -98,6 +98,20 @@ def _stage_parallel_fft(x: ComplexTensor, num_cores: int, inverse: bool) -> Comp
     n1, n2 = _factorize(n)
     sign = 1.0 if inverse else -1.0
     (xr, xi), restore = place(x.real.reshape(n), x.imag.reshape(n))
+    if n & (n - 1) == 0 and n > 1024 and n1 <= (1 << 20) and xr.dtype == torch.float32:
+        # powers of two: the column transforms read the [n1][n2] view in place and multiply by
+        # the twiddle W_N^{l k1} in their last pass (trnfft_exec_c2c_axis_tw), so neither the
+        # transposed copy nor N-sized twiddle tables are built
+        from .. import _lib
+
+        yr = torch.empty(n1, n2, dtype=torch.float32, device=xr.device)
+        yi = torch.empty_like(yr)
+        plan = _lib.device_plan(n1, xr.device)
+        twp = _lib.device_plan(n, xr.device)
+        _lib.call("trnfft_exec_c2c_axis_tw", plan.handle, twp.handle, _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(yr),
+                  _lib.ptr(yi), 1, n2, 0, 0, int(bool(inverse)), 0, _lib.stream_ptr(xr.device))
+        row = _batch_split_fft(ComplexTensor(yr, yi), inverse=inverse, num_cores=num_cores)
+        return ComplexTensor(restore(row.real.T.contiguous().reshape(n)), restore(row.imag.T.contiguous().reshape(n)))
     col = _batch_split_fft(
         ComplexTensor(xr.reshape(n1, n2).T.contiguous(), xi.reshape(n1, n2).T.contiguous()),
         inverse=inverse, num_cores=num_cores,
