@@ -635,6 +635,51 @@ class SmallNGemm(SmallN):
         self.tensor_flops = sum(3 * 8.0 * self.batch * n * n for n in (256,))
 
 
+class RealRoundTrip(Workload):
+    """BASELINE configs[3] real part: rfft then irfft of 4096 real rows of n = 4093."""
+
+    metric = "batched real FFT GFLOP/s (2.5N*log2N per real transform), rfft+irfft round trip"
+
+    def __init__(self, n=4093, batch=4096):
+        self.n, self.batch = n, batch
+        self.name = f"rfft + irfft round trip, real fp32 rows of N={n}, batch={batch} (configs[3])"
+        self.work = 2 * 2.5 * n * math.log2(n) * batch
+        self.dom_bytes = 4.0 * n * batch + 8.0 * (n // 2 + 1) * batch  # one direction: real in, bins out
+        self.dominant = f"real-input Bluestein kernel (two rows per transform), N={n}"
+
+    def setup(self, dev, g):
+        import trnfft_b200 as trnfft
+
+        self.x = torch.randn(self.batch, self.n, device=dev, generator=g)
+        self.step = lambda: trnfft.irfft(trnfft.rfft(self.x), n=self.n)
+        self.launches = {"rfft": lambda: trnfft.rfft(self.x)}
+        self.launches_per_step = 2
+        self.inputs = [self.x]
+        self.e2e_fn = lambda ts: [trnfft.irfft(trnfft.rfft(ts[0]), n=self.n)]
+
+    def check(self, out):
+        return rel_err(out, self.x)
+
+    def ref_full_units(self):
+        return self.batch
+
+    def ref_sample(self, T, units):
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(units, self.n, generator=g)
+        return (lambda: T.irfft(T.rfft(x), n=self.n)), 2 * 2.5 * self.n * math.log2(self.n) * units, \
+            f"{units} of {self.batch} rows"
+
+    def cpu_sample(self, threads, rows):
+        from oracle import trnfft_oracle as O
+
+        rng = np.random.default_rng(0)
+        x = rng.standard_normal((max(1, rows // 32), self.n)).astype(np.float32)
+        t0 = time.perf_counter()
+        yr, yi = O.rfft(x)
+        O.irfft(yr, yi, n=self.n)
+        return time.perf_counter() - t0, 2 * 2.5 * self.n * math.log2(self.n) * x.shape[0]
+
+
 class Istft(Workload):
     """Inverse of BASELINE configs[2]: istft of the 256 x 257 x 626 spectrogram back to 256 x 160000
     samples (n_fft 512, hop 256, periodic Hann, centred), one fused kernel."""
@@ -785,6 +830,7 @@ WORKLOADS = {
     "fft2": Fft2,
     "rows8192": lambda: C2CRoundTrip(8192, 8192, "one-pass rows of 8192 points (k_c2c_big)"),
     "rows16384": lambda: C2CRoundTrip(16384, 4096, "one-pass rows of 16384 points (k_c2c_big), the fft2 / four-step row pass"),
+    "rfft4093": RealRoundTrip,
     "istft": Istft,
     "mask": MaskApply,
     "double4093": lambda: C2CDouble(4093, 4096, "BASELINE configs[3], precision double"),

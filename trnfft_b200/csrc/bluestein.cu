@@ -41,7 +41,11 @@ struct BlueGeom {
   static constexpr size_t smem = (size_t)G * MP * sizeof(float2);
 };
 
-// MODE 0: C2C, MODE 1: R2C (real rows -> n/2+1 bins), MODE 2: C2R (n/2+1 bins -> real rows)
+// MODE 0: C2C, MODE 1: R2C (real rows -> n/2+1 bins), MODE 2: C2R (n/2+1 bins -> real rows).
+// The real modes transform two rows at once: rows a = 2t and b = 2t+1 go in as
+// a + i b (R2C; the two spectra are separated on chip from Z_k and Z_{n-k}),
+// or their spectra as A + i B (C2R; the real and imaginary parts of the result
+// are the two rows), half the work of a complex transform per row.
 template <int LOGM, bool INV, int MODE, int LE_ = BlueLogE<LOGM>::v>
 __global__ void __launch_bounds__(BlueGeom<LOGM, LE_>::THREADS, BlueGeom<LOGM, LE_>::MINB) k_bluestein(BlueArgs a) {
   using GM = BlueGeom<LOGM, LE_>;
@@ -52,8 +56,12 @@ __global__ void __launch_bounds__(BlueGeom<LOGM, LE_>::THREADS, BlueGeom<LOGM, L
   const int g = threadIdx.x / S::T;
   const int j = threadIdx.x % S::T;
   const long long t = (long long)blockIdx.x * GM::G + g;
-  const bool valid = t < a.batch;
+  // the real modes pack rows 2t and 2t+1 into one complex transform
+  const long long ntf = MODE == 0 ? a.batch : (a.batch + 1) / 2;
+  const bool valid = t < ntf;
   const long long tt = valid ? t : 0;
+  const long long row0 = MODE == 0 ? tt : 2 * tt;
+  const bool has1 = MODE != 0 && row0 + 1 < a.batch;
   const int n = a.n;
   const int half = n / 2;
   float2* sb = reinterpret_cast<float2*>(sm) + g * GM::MP;
@@ -72,20 +80,25 @@ __global__ void __launch_bounds__(BlueGeom<LOGM, LE_>::THREADS, BlueGeom<LOGM, L
       xr = __ldg(a.xr + tt * n + i);
       xi = __ldg(a.xi + tt * n + i);
     } else if constexpr (MODE == 1) {
-      xr = __ldg(a.xr + tt * n + i);
-      xi = 0.f;
+      // z = a + i b for the real rows a = 2t, b = 2t+1
+      xr = __ldg(a.xr + row0 * n + i);
+      xi = has1 ? __ldg(a.xr + (row0 + 1) * n + i) : 0.f;
     } else {
-      // Hermitian extension of the n/2+1 input bins (trnfft/api.py:54-66);
-      // only the real part of the result is kept, so the imaginary parts of
-      // bin 0 and (even n) bin n/2 are dropped.
+      // Z = A + i B for the Hermitian extensions A, B of rows 2t, 2t+1 (trnfft/api.py:54-66);
+      // the imaginary parts of bin 0 and (even n) bin n/2 do not contribute to a real result
       const long long h = half + 1;
-      if (i <= half) {
-        xr = __ldg(a.xr + tt * h + i);
-        xi = (i == 0 || 2 * i == n) ? 0.f : __ldg(a.xi + tt * h + i);
-      } else {
-        xr = __ldg(a.xr + tt * h + (n - i));
-        xi = -__ldg(a.xi + tt * h + (n - i));
+      const int src = i <= half ? i : n - i;
+      const float sg = i <= half ? 1.f : -1.f;
+      const bool im_ok = !(src == 0 || 2 * src == n);
+      const float ar = __ldg(a.xr + row0 * h + src);
+      const float ai = im_ok ? sg * __ldg(a.xi + row0 * h + src) : 0.f;
+      float br = 0.f, bi = 0.f;
+      if (has1) {
+        br = __ldg(a.xr + (row0 + 1) * h + src);
+        bi = im_ok ? sg * __ldg(a.xi + (row0 + 1) * h + src) : 0.f;
       }
+      xr = ar - bi;
+      xi = ai + br;
     }
     const float2 c = __ldg(chirp + i);
     const float ci = csign * c.y;
@@ -123,11 +136,9 @@ __global__ void __launch_bounds__(BlueGeom<LOGM, LE_>::THREADS, BlueGeom<LOGM, L
   smem_passes<LOGM, LE, true, 0, S::P - 1>(j, sb);
   pass_load<LOGM, LE, S::P - 1>(j, vr, vi, sload);
   const float sc = INV ? 1.f / (float)n : 1.f;
+  if constexpr (MODE == 1) __syncthreads();  // sb is rewritten below with the packed spectrum
   pass_compute_store<LOGM, LE, S::P - 1, true>(j, vr, vi, [&](int i, float r, float m) {
     if (!valid || i >= n) return;
-    if constexpr (MODE == 1) {
-      if (i > half) return;
-    }
     const float2 c = __ldg(chirp + i);
     const float ci = csign * c.y;
     const float yr = fmaf(r, c.x, -m * ci) * sc;
@@ -136,13 +147,29 @@ __global__ void __launch_bounds__(BlueGeom<LOGM, LE_>::THREADS, BlueGeom<LOGM, L
       a.yr[tt * n + i] = yr;
       a.yi[tt * n + i] = yi;
     } else if constexpr (MODE == 1) {
-      const long long h = half + 1;
-      a.yr[tt * h + i] = yr;
-      a.yi[tt * h + i] = yi;
+      sb[spad<S::SH>(i)] = make_float2(yr, yi);
     } else {
-      a.yr[tt * n + i] = yr;
+      a.yr[row0 * n + i] = yr;
+      if (has1) a.yr[(row0 + 1) * n + i] = yi;
     }
   });
+  if constexpr (MODE == 1) {
+    // Z = FFT(a + i b): A_k = (Z_k + conj Z_{n-k}) / 2, B_k = (Z_k - conj Z_{n-k}) / (2i)
+    __syncthreads();
+    if (valid) {
+      const long long h = half + 1;
+      for (int k = j; k <= half; k += S::T) {
+        const float2 z = sb[spad<S::SH>(k)];
+        const float2 w = sb[spad<S::SH>(k == 0 ? 0 : n - k)];
+        a.yr[row0 * h + k] = 0.5f * (z.x + w.x);
+        a.yi[row0 * h + k] = 0.5f * (z.y - w.y);
+        if (has1) {
+          a.yr[(row0 + 1) * h + k] = 0.5f * (z.y + w.y);
+          a.yi[(row0 + 1) * h + k] = 0.5f * (w.x - z.x);
+        }
+      }
+    }
+  }
 }
 
 template <int LOGM, bool INV, int MODE, int LE_ = BlueLogE<LOGM>::v>
@@ -153,7 +180,8 @@ static cudaError_t launch_blue_t(const BlueArgs& a, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
     if (e != cudaSuccess) return e;
   }
-  const long long blocks = (a.batch + GM::G - 1) / GM::G;
+  const long long ntf = MODE == 0 ? a.batch : (a.batch + 1) / 2;  // real modes: two rows per transform
+  const long long blocks = (ntf + GM::G - 1) / GM::G;
   kern<<<(unsigned)blocks, GM::THREADS, GM::smem, st>>>(a);
   return cudaGetLastError();
 }
