@@ -139,3 +139,35 @@ def test_complex_layers_off_the_hot_path_match_their_definitions():
     ref = torch.nn.BatchNorm1d(3)
     assert torch.allclose(v.real, ref(u.real), atol=1e-6)
     assert torch.allclose(v.imag, torch.nn.BatchNorm1d(3)(u.imag), atol=1e-6)
+
+
+def test_istft_out_len_matches_the_reference_trim_rules():
+    """The fused iSTFT's output length rule (api.py:454-468) against the oracle's istft."""
+    import numpy as np
+
+    from oracle import trnfft_oracle as O
+    from trnfft_b200._ops import istft_out_len
+
+    rng = np.random.default_rng(0)
+    for n_fft, hop, frames, center, length in [(16, 4, 9, True, None), (16, 4, 9, False, None),
+                                                (16, 16, 3, True, None), (8, 3, 5, True, 30),
+                                                (8, 3, 5, True, 2), (4, 1, 2, True, None)]:
+        bins = n_fft // 2 + 1
+        sr = rng.standard_normal((bins, frames)).astype(np.float32)
+        si = rng.standard_normal((bins, frames)).astype(np.float32)
+        want = O.istft(sr, si, n_fft, hop, window=np.ones(n_fft, np.float32), center=center, length=length)
+        assert istft_out_len(n_fft, frames, hop, center, length) == want.shape[-1]
+
+
+def test_mask_period_and_row_chunks():
+    from trnfft_b200.nki.dispatch import _mask_period
+    from trnfft_b200.streaming import _chunks
+
+    assert _mask_period((257, 100), (4, 257, 100)) == 257 * 100
+    assert _mask_period((1, 1, 7), (3, 5, 7)) == 7
+    assert _mask_period((3, 1, 7), (3, 5, 7)) is None
+    assert _mask_period((4, 257, 100), (257, 100)) is None
+    for rows, n in [(10, 4), (3, 8), (8192, 4), (1, 1)]:
+        parts = list(_chunks(rows, max(1, min(n, rows))))
+        assert parts[0][0] == 0 and parts[-1][1] == rows
+        assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
