@@ -93,3 +93,29 @@ def test_dft_as_gemm_large_batch_vs_fp64():
     finally:
         trnfft.set_small_n_algorithm("stockham")
     assert rel_l2(cplx(y), np.fft.fft(x.astype(np.complex128))) < 2e-6
+
+
+def test_complex_linear_on_a_second_device_after_the_first():
+    """The GEMM's shared-memory opt-in is per device: a layer on cuda:1 after one on cuda:0
+    (same process) must launch and agree with fp64 (needs two GPUs)."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        import pytest
+
+        pytest.skip("needs two GPUs")
+    from trnfft_b200 import ComplexTensor
+    from trnfft_b200.nn import ComplexLinear
+
+    for dev in ("cuda:0", "cuda:1"):
+        torch.manual_seed(3)
+        layer = ComplexLinear(512, 256).to(dev)
+        x = ComplexTensor(torch.randn(300, 512, device=dev), torch.randn(300, 512, device=dev))
+        with torch.no_grad():
+            y = layer(x)
+        wr, wi = layer.W_re.weight.double(), layer.W_im.weight.double()
+        a, b = x.real.double(), x.imag.double()
+        ref = torch.complex(a @ wr.t() - b @ wi.t(), a @ wi.t() + b @ wr.t())
+        got = torch.complex(y.real.double(), y.imag.double())
+        assert y.real.device == torch.device(dev)
+        assert float(torch.linalg.vector_norm(got - ref) / torch.linalg.vector_norm(ref)) < 1e-5
