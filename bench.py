@@ -1115,6 +1115,7 @@ def run_ours(args, world, rank, local):
         if world > 1:
             extras["multi_gpu_check_rel_l2"] = multi_gpu_check(world, rank, dev)
         extras["large_four_step"] = large_extra(world, rank, dev)
+        extras["fft2_16384_sharded"] = fft2_extra(world, rank, dev)
 
     if rank != 0:
         return
@@ -1285,6 +1286,56 @@ def large_extra(world, rank, dev, steps=10, warmup=3, logn=30):
         res["speedup_vs_1gpu"] = round(ms1 / res["ms"], 3)
         res["gflops"] = round(c2c_flops(n, 1) / (res["ms"] / 1e3) / 1e9, 1)
         del x, xr, xi
+        torch.cuda.empty_cache()
+    barrier(world)
+    return res
+
+
+def fft2_extra(world, rank, dev, side=16384, steps=10, warmup=3):
+    """fft2 of a side x side field sharded by rows over `world` GPUs (fft2_distributed, natural
+    row layout; max over ranks of the CUDA-event time) and, on rank 0, trnfft.fft2 of the whole
+    field on one GPU."""
+    import trnfft_b200 as trnfft
+    from trnfft_b200 import ComplexTensor
+    from trnfft_b200 import distributed as D
+
+    st = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+
+    def time_fn(fn, collective):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if collective:
+            barrier(world)
+        ts = []
+        for _ in range(steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sum(ts) / len(ts)
+
+    res = {"side": side, "steps": steps}
+    if world > 1:
+        hr = side // world
+        x = ComplexTensor(torch.randn(hr, side, device=dev, generator=g), torch.randn(hr, side, device=dev, generator=g))
+        res["ms"] = round(allreduce_max(time_fn(lambda: D.fft2_distributed(x), True), world), 4)
+        del x
+        D.clear_exchanges()
+        torch.cuda.empty_cache()
+    barrier(world)
+    if rank == 0:
+        x = ComplexTensor(torch.randn(side, side, device=dev, generator=g),
+                          torch.randn(side, side, device=dev, generator=g))
+        res["ms_1gpu"] = round(time_fn(lambda: trnfft.fft2(x), False), 4)
+        if world == 1:
+            res["ms"] = res["ms_1gpu"]
+        res["speedup_vs_1gpu"] = round(res["ms_1gpu"] / res["ms"], 3)
+        res["gflops"] = round(2 * c2c_flops(side, side) / (res["ms"] / 1e3) / 1e9, 1)
+        del x
         torch.cuda.empty_cache()
     barrier(world)
     return res

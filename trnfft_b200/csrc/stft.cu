@@ -11,16 +11,18 @@
 // z[n] = x[2n] + i x[2n+1] plus an on-chip split, and writes the bins in the
 // (freq, time) layout: a block owns G consecutive frames of one waveform, so
 // each frequency row receives G contiguous floats per store.
+#include <cstdlib>
+
 #include "fft_common.cuh"
 #include "kernels.h"
 
 namespace tfb {
 
-template <int LOGM>
+template <int LOGM, int TB = 128>
 struct StftGeom {
   static constexpr int LE = 4;
   using S = Sched<LOGM, LE>;
-  static constexpr int G0 = 128 / S::T;
+  static constexpr int G0 = TB / S::T;
   static constexpr int G = G0 < 1 ? 1 : G0;  // frames per block
   static constexpr int THREADS = G * S::T;
   static constexpr int MINB = THREADS >= 1024 ? 1 : 1024 / THREADS;
@@ -49,9 +51,9 @@ __device__ __forceinline__ long long stft_src(long long i, long long L, int mode
   }
 }
 
-template <int LOGM>
-__global__ void __launch_bounds__(StftGeom<LOGM>::THREADS, StftGeom<LOGM>::MINB) k_stft(StftArgs a) {
-  using GM = StftGeom<LOGM>;
+template <int LOGM, int TB>
+__global__ void __launch_bounds__(StftGeom<LOGM, TB>::THREADS, StftGeom<LOGM, TB>::MINB) k_stft(StftArgs a) {
+  using GM = StftGeom<LOGM, TB>;
   using S = typename GM::S;
   constexpr int M = S::N;
   constexpr int N = 2 * M;
@@ -130,10 +132,21 @@ __global__ void __launch_bounds__(StftGeom<LOGM>::THREADS, StftGeom<LOGM>::MINB)
   }
 }
 
-template <int LOGM>
-static cudaError_t launch_stft_t(const StftArgs& a, cudaStream_t st) {
-  using GM = StftGeom<LOGM>;
-  auto kern = k_stft<LOGM>;
+// TRNFFT_B200_STFT_THREADS (128, 256 or 512) sets the frames per block (threads / (n_fft/32)),
+// for measurement; 128 by default.
+static int stft_block_threads() {
+  static const int v = [] {
+    const char* e = getenv("TRNFFT_B200_STFT_THREADS");
+    const int t = e ? atoi(e) : 128;
+    return (t == 256 || t == 512) ? t : 128;
+  }();
+  return v;
+}
+
+template <int LOGM, int TB>
+static cudaError_t launch_stft_tb(const StftArgs& a, cudaStream_t st) {
+  using GM = StftGeom<LOGM, TB>;
+  auto kern = k_stft<LOGM, TB>;
   if (GM::smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
     if (e != cudaSuccess) return e;
@@ -143,6 +156,15 @@ static cudaError_t launch_stft_t(const StftArgs& a, cudaStream_t st) {
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   kern<<<(unsigned)blocks, GM::THREADS, GM::smem, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int LOGM>
+static cudaError_t launch_stft_t(const StftArgs& a, cudaStream_t st) {
+  switch (stft_block_threads()) {
+    case 256: return launch_stft_tb<LOGM, 256>(a, st);
+    case 512: return launch_stft_tb<LOGM, 512>(a, st);
+    default: return launch_stft_tb<LOGM, 128>(a, st);
+  }
 }
 
 cudaError_t launch_stft(int logn, const StftArgs& a, cudaStream_t st) {
