@@ -201,7 +201,9 @@ __device__ __forceinline__ void mix_pass_r(int code, const float2* src, float2* 
   }
 }
 
-// MODE 0: C2C; MODE 1: R2C (real rows -> n/2+1 bins); MODE 2: C2R (n/2+1 bins -> real rows)
+// MODE 0: C2C; MODE 1: R2C (real rows -> n/2+1 bins); MODE 2: C2R (n/2+1 bins -> real rows).
+// The real modes transform two rows at once (a + i b in, the two spectra separated on chip;
+// or A + i B in, real and imaginary parts out as the two rows).
 template <int LOGNMAX, bool INV, int MODE>
 __global__ void __launch_bounds__(MixGeom<LOGNMAX>::THREADS, MixGeom<LOGNMAX>::MINB) k_mixed(MixedArgs a) {
   using GM = MixGeom<LOGNMAX>;
@@ -210,8 +212,12 @@ __global__ void __launch_bounds__(MixGeom<LOGNMAX>::THREADS, MixGeom<LOGNMAX>::M
   const int j0 = threadIdx.x % GM::T;
   const int n = a.n;
   const long long t = (long long)blockIdx.x * GM::G + g;
-  const bool valid = t < a.batch;
+  // the real modes pack rows 2t and 2t+1 into one complex transform
+  const long long ntf = MODE == 0 ? a.batch : (a.batch + 1) / 2;
+  const bool valid = t < ntf;
   const long long tt = valid ? t : 0;
+  const long long row0 = MODE == 0 ? tt : 2 * tt;
+  const bool has1 = MODE != 0 && row0 + 1 < a.batch;
   float2* buf0 = sm2 + g * 2 * a.pitch;
   float2* buf1 = buf0 + a.pitch;
   const int half = n / 2;
@@ -224,32 +230,38 @@ __global__ void __launch_bounds__(MixGeom<LOGNMAX>::THREADS, MixGeom<LOGNMAX>::M
       r = __ldg(a.xr + tt * n + i);
       m = __ldg(a.xi + tt * n + i);
     } else if constexpr (MODE == 1) {
-      r = __ldg(a.xr + tt * n + i);
+      // z = a + i b for the real rows a = 2t, b = 2t+1
+      r = __ldg(a.xr + row0 * n + i);
+      m = has1 ? __ldg(a.xr + (row0 + 1) * n + i) : 0.f;
     } else {
-      // Hermitian extension of bins 0..n/2 (trnfft/api.py:54-66); only the real
-      // part of the result is kept, so the imaginary parts of bin 0 and (even n)
-      // bin n/2 do not contribute
-      if (i <= half) {
-        r = __ldg(a.xr + tt * hbins + i);
-        m = (i == 0 || 2 * i == n) ? 0.f : __ldg(a.xi + tt * hbins + i);
-      } else {
-        r = __ldg(a.xr + tt * hbins + (n - i));
-        m = -__ldg(a.xi + tt * hbins + (n - i));
+      // Z = A + i B for the Hermitian extensions A, B of rows 2t, 2t+1 (trnfft/api.py:54-66);
+      // the imaginary parts of bin 0 and (even n) bin n/2 do not contribute to a real result
+      const int src = i <= half ? i : n - i;
+      const float sg = i <= half ? 1.f : -1.f;
+      const bool im_ok = !(src == 0 || 2 * src == n);
+      const float ar = __ldg(a.xr + row0 * hbins + src);
+      const float ai = im_ok ? sg * __ldg(a.xi + row0 * hbins + src) : 0.f;
+      float br = 0.f, bi = 0.f;
+      if (has1) {
+        br = __ldg(a.xr + (row0 + 1) * hbins + src);
+        bi = im_ok ? sg * __ldg(a.xi + (row0 + 1) * hbins + src) : 0.f;
       }
+      r = ar - bi;
+      m = ai + br;
     }
   };
+  float2* zb = buf1;  // MODE 1: the packed spectrum Z is gathered here before the split
   auto st = [&](int i, float r, float m) {
-    if (!valid) return;
     if constexpr (MODE == 0) {
+      if (!valid) return;
       a.yr[tt * n + i] = r * a.scale;
       a.yi[tt * n + i] = m * a.scale;
     } else if constexpr (MODE == 1) {
-      if (i <= half) {
-        a.yr[tt * hbins + i] = r;
-        a.yi[tt * hbins + i] = m;
-      }
+      zb[mpad(i)] = make_float2(r, m);
     } else {
-      a.yr[tt * n + i] = r * a.scale;
+      if (!valid) return;
+      a.yr[row0 * n + i] = r * a.scale;
+      if (has1) a.yr[(row0 + 1) * n + i] = m * a.scale;
     }
   };
   const int P = a.npass;
@@ -257,27 +269,44 @@ __global__ void __launch_bounds__(MixGeom<LOGNMAX>::THREADS, MixGeom<LOGNMAX>::M
   int code = (int)(codes & 7);
   if (P == 1) {
     mix_pass_r<INV, LOGNMAX, true, true>(code, buf0, buf1, j0, n, 1, a.tw, ld, st);
-    return;
-  }
-  // per-pass twiddle blocks follow each other: pass p takes ns_p * (R_p - 1) entries
-  int ns = 1;
-  long long off = 0;
-  mix_pass_r<INV, LOGNMAX, true, false>(code, buf1, buf0, j0, n, ns, a.tw + off, ld, st);
-  off += (long long)ns * (mix_radix_of(code) - 1);
-  ns *= mix_radix_of(code);
-  float2* src = buf0;
-  float2* dst = buf1;
-  for (int p = 1; p < P - 1; ++p) {
-    code = (int)((codes >> (3 * p)) & 7);
-    mix_pass_r<INV, LOGNMAX, false, false>(code, src, dst, j0, n, ns, a.tw + off, ld, st);
+  } else {
+    // per-pass twiddle blocks follow each other: pass p takes ns_p * (R_p - 1) entries
+    int ns = 1;
+    long long off = 0;
+    mix_pass_r<INV, LOGNMAX, true, false>(code, buf1, buf0, j0, n, ns, a.tw + off, ld, st);
     off += (long long)ns * (mix_radix_of(code) - 1);
     ns *= mix_radix_of(code);
-    float2* t = src;
-    src = dst;
-    dst = t;
+    float2* src = buf0;
+    float2* dst = buf1;
+    for (int p = 1; p < P - 1; ++p) {
+      code = (int)((codes >> (3 * p)) & 7);
+      mix_pass_r<INV, LOGNMAX, false, false>(code, src, dst, j0, n, ns, a.tw + off, ld, st);
+      off += (long long)ns * (mix_radix_of(code) - 1);
+      ns *= mix_radix_of(code);
+      float2* tmp = src;
+      src = dst;
+      dst = tmp;
+    }
+    zb = dst;  // the last pass reads src; MODE 1 writes Z into the other row buffer
+    code = (int)((codes >> (3 * (P - 1))) & 7);
+    mix_pass_r<INV, LOGNMAX, false, true>(code, src, dst, j0, n, ns, a.tw + off, ld, st);
   }
-  code = (int)((codes >> (3 * (P - 1))) & 7);
-  mix_pass_r<INV, LOGNMAX, false, true>(code, src, dst, j0, n, ns, a.tw + off, ld, st);
+  if constexpr (MODE == 1) {
+    // Z = FFT(a + i b): A_k = (Z_k + conj Z_{n-k}) / 2, B_k = (Z_k - conj Z_{n-k}) / (2i)
+    __syncthreads();
+    if (valid) {
+      for (int k = j0; k <= half; k += GM::T) {
+        const float2 z = zb[mpad(k)];
+        const float2 w = zb[mpad(k == 0 ? 0 : n - k)];
+        a.yr[row0 * hbins + k] = 0.5f * (z.x + w.x);
+        a.yi[row0 * hbins + k] = 0.5f * (z.y - w.y);
+        if (has1) {
+          a.yr[(row0 + 1) * hbins + k] = 0.5f * (z.y + w.y);
+          a.yi[(row0 + 1) * hbins + k] = 0.5f * (w.x - z.x);
+        }
+      }
+    }
+  }
 }
 
 template <int LOGNMAX, bool INV, int MODE>
@@ -290,7 +319,8 @@ static cudaError_t launch_mixed_t(MixedArgs a, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  const long long blocks = (a.batch + GM::G - 1) / GM::G;
+  const long long ntf = MODE == 0 ? a.batch : (a.batch + 1) / 2;  // real modes: two rows per transform
+  const long long blocks = (ntf + GM::G - 1) / GM::G;
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   kern<<<(unsigned)blocks, GM::THREADS, smem, st>>>(a);
