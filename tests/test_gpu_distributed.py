@@ -60,7 +60,9 @@ def _worker(rank, world, port, q):
     res["fft2_cols"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
     g = D.fft2_distributed(fl, exchange="nccl")
     res["fft2_nccl"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
-    g = D.fft2_distributed(fl)  # second peer call reuses the mapped planes
+    g = D.fft2_distributed(fl, chunks=4)  # row chunks sent while the next chunk computes
+    res["fft2_ch"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
+    g = D.fft2_distributed(fl)  # another peer call reuses the mapped planes
     res["fft2_2"] = (g.real.cpu().numpy(), g.imag.cpu().numpy())
     torch.cuda.synchronize()
     q.put((rank, res))
@@ -106,5 +108,6 @@ def test_two_gpu_four_step_and_fft2():
     assert rel(cat("fft2"), F) < 2e-6
     assert rel(cat("fft2_nccl"), F) < 2e-6
     assert rel(cat("fft2_2"), F) < 2e-6
+    assert rel(cat("fft2_ch"), F) < 2e-6
     cols = np.concatenate([out[r]["fft2_cols"][0] + 1j * out[r]["fft2_cols"][1] for r in range(world)], axis=1)
     assert rel(cols, F) < 2e-6

@@ -431,7 +431,7 @@ def _fft2_exchange(xr, xi, group, inverse, natural_order, row_fft, col_fft):
     return br.permute(1, 0, 2).reshape(hr, w).contiguous(), bi.permute(1, 0, 2).reshape(hr, w).contiguous()
 
 
-def _fft2_peer(xr, xi, group, inverse, natural_order):
+def _fft2_peer(xr, xi, group, inverse, natural_order, chunks=1):
     """fft2 of row blocks [H/P][W] with the exchanges as 2-D peer copies (copy engines over NVLink).
 
     Row transforms; every rank copies its column block q of its rows straight into rank q's
@@ -457,12 +457,39 @@ def _fft2_peer(xr, xi, group, inverse, natural_order):
         _exchanges[key] = (group, cols_ex, back_ex)
     st = _lib.stream_ptr(dev)
     di = dev.index
-    yr, yi = _ops.c2c_raw(xr, xi, inverse)  # rows, [hr][w]
-    _device_barrier(group, dev)  # every rank is done reading its receive planes
-    for q in range(P):
-        for src, dst in ((yr, cols_ex.peer_re[q]), (yi, cols_ex.peer_im[q])):
-            _lib.call("trnfft_copy2d", ctypes.c_void_p(dst + 4 * p * hr * cw), cw * 4,
-                      ctypes.c_void_p(src.data_ptr() + 4 * q * cw), w * 4, cw * 4, hr, di, st)
+    nch = chunks if (chunks > 1 and hr % chunks == 0) else 1
+    rc = hr // nch
+    if nch == 1:
+        yr, yi = _ops.c2c_raw(xr, xi, inverse)  # rows, [hr][w]
+        _device_barrier(group, dev)  # every rank is done reading its receive planes
+    else:
+        _device_barrier(group, dev)
+        yr = torch.empty(hr, w, dtype=torch.float32, device=dev)
+        yi = torch.empty_like(yr)
+        rplan = _lib.device_plan(w, dev)
+        main = torch.cuda.current_stream(dev)
+        side = _side_streams.get(("copy", dev.index))
+        if side is None:
+            side = _side_streams[("copy", dev.index)] = torch.cuda.Stream(device=dev)
+        side.wait_stream(main)
+    for c in range(nch):
+        if nch > 1:
+            # rows of chunk c on the compute stream; their copies on a second stream, so the copy
+            # engines move chunk c over NVLink while the SMs transform chunk c+1
+            off = 4 * c * rc * w
+            _lib.call("trnfft_exec_c2c", rplan.handle, ctypes.c_void_p(xr.data_ptr() + off),
+                      ctypes.c_void_p(xi.data_ptr() + off), ctypes.c_void_p(yr.data_ptr() + off),
+                      ctypes.c_void_p(yi.data_ptr() + off), rc, int(bool(inverse)), None, st)
+            side.wait_stream(main)
+            cst = ctypes.c_void_p(side.cuda_stream)
+        else:
+            cst = st
+        for q in range(P):
+            for src, dst in ((yr, cols_ex.peer_re[q]), (yi, cols_ex.peer_im[q])):
+                _lib.call("trnfft_copy2d", ctypes.c_void_p(dst + 4 * (p * hr + c * rc) * cw), cw * 4,
+                          ctypes.c_void_p(src.data_ptr() + 4 * (c * rc * w + q * cw)), w * 4, cw * 4, rc, di, cst)
+    if nch > 1:
+        main.wait_stream(side)
     _device_barrier(group, dev)  # every block has landed
     zr = torch.empty(h, cw, dtype=torch.float32, device=dev)
     zi = torch.empty_like(zr)
@@ -485,13 +512,14 @@ def _fft2_peer(xr, xi, group, inverse, natural_order):
 
 
 def fft2_distributed(x_local: ComplexTensor, inverse: bool = False, natural_order: bool = True,
-                     group=None, exchange: str = "peer") -> ComplexTensor:
+                     group=None, exchange: str = "peer", chunks: int = 1) -> ComplexTensor:
     """fft2 of an [H][W] field whose rows are split evenly over the ranks ([H/P][W] each).
 
     ``exchange="peer"`` (default on one node, up to 8 ranks, power-of-two H): 2-D peer copies into
     CUDA-IPC-mapped planes (``_fft2_peer``); ``exchange="nccl"``: NCCL all-to-all with the
-    transposes around it.  The result is [H/P][W] rows (``natural_order``) or the column block
-    [H][W/P] of this rank."""
+    transposes around it.  ``chunks`` > 1 (peer exchange) transforms the rows in that many chunks
+    and sends each chunk on a second stream while the next one computes.  The result is [H/P][W]
+    rows (``natural_order``) or the column block [H][W/P] of this rank."""
     P, _ = _world(group)
     xr = x_local.real.float().contiguous()
     xi = x_local.imag.float().contiguous()
@@ -500,7 +528,7 @@ def fft2_distributed(x_local: ComplexTensor, inverse: bool = False, natural_orde
     if w % P:
         raise ValueError("fft2_distributed: the width must split evenly over the ranks")
     if exchange == "peer" and P <= 8 and xr.is_cuda and h & (h - 1) == 0 and h <= (1 << 20):
-        zr, zi = _fft2_peer(xr, xi, group, inverse, natural_order)
+        zr, zi = _fft2_peer(xr, xi, group, inverse, natural_order, chunks)
     else:
         zr, zi = _fft2_exchange(xr, xi, group, inverse, natural_order, _cuda_row_fft, _cuda_col_fft)
     return ComplexTensor(zr, zi)
