@@ -1323,7 +1323,7 @@ def fft2_extra(world, rank, dev, side=16384, steps=10, warmup=3):
         hr = side // world
         x = ComplexTensor(torch.randn(hr, side, device=dev, generator=g), torch.randn(hr, side, device=dev, generator=g))
         res["ms"] = round(allreduce_max(time_fn(lambda: D.fft2_distributed(x), True), world), 4)
-        res["ms_row_chunks4"] = round(allreduce_max(time_fn(lambda: D.fft2_distributed(x, chunks=4), True), world), 4)
+        res["ms_unchunked"] = round(allreduce_max(time_fn(lambda: D.fft2_distributed(x, chunks=1), True), world), 4)
         del x
         D.clear_exchanges()
         torch.cuda.empty_cache()

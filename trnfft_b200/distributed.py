@@ -512,13 +512,14 @@ def _fft2_peer(xr, xi, group, inverse, natural_order, chunks=1):
 
 
 def fft2_distributed(x_local: ComplexTensor, inverse: bool = False, natural_order: bool = True,
-                     group=None, exchange: str = "peer", chunks: int = 1) -> ComplexTensor:
+                     group=None, exchange: str = "peer", chunks: int = 4) -> ComplexTensor:
     """fft2 of an [H][W] field whose rows are split evenly over the ranks ([H/P][W] each).
 
     ``exchange="peer"`` (default on one node, up to 8 ranks, power-of-two H): 2-D peer copies into
     CUDA-IPC-mapped planes (``_fft2_peer``); ``exchange="nccl"``: NCCL all-to-all with the
-    transposes around it.  ``chunks`` > 1 (peer exchange) transforms the rows in that many chunks
-    and sends each chunk on a second stream while the next one computes.  The result is [H/P][W]
+    transposes around it.  ``chunks`` (default 4; peer exchange) transforms the rows in that many
+    chunks and sends each chunk on a second stream while the next one computes (4 GPUs, 16384^2:
+    3.70 ms against 3.86 ms unchunked).  The result is [H/P][W]
     rows (``natural_order``) or the column block [H][W/P] of this rank."""
     P, _ = _world(group)
     xr = x_local.real.float().contiguous()
