@@ -226,8 +226,11 @@ static cudaError_t launch_blue_t(const BlueArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// TRNFFT_B200_BLUE_LOGE=4 runs the m >= 8192 sizes with 16 values per thread
-// (twice the threads, half the registers each) for measurement.
+// Values per thread for m >= 8192: C2C keeps 32 (radix-32 passes); the packed real modes at
+// m = 8192 use 16 (twice the threads, half the registers each), measured on B200 with the tables
+// in shared memory: rfft n = 4093 batch 4096 0.205 ms per launch against 0.252 ms with 32, while
+// C2C measured the same either way (0.284 / 0.279 ms).  TRNFFT_B200_BLUE_LOGE=4 or 5 forces one
+// choice for every mode, for measurement.
 static int blue_loge_override() {
   static const int v = [] {
     const char* e = getenv("TRNFFT_B200_BLUE_LOGE");
@@ -239,7 +242,8 @@ static int blue_loge_override() {
 template <int LOGM>
 static cudaError_t launch_blue_m(int mode, bool inv, const BlueArgs& a, cudaStream_t st) {
   if constexpr (LOGM >= 13) {
-    if (blue_loge_override() == 4) {
+    const int ov = blue_loge_override();
+    if (ov == 4 || (ov != 5 && LOGM == 13 && mode != 0)) {
       switch (mode) {
         case 0: return inv ? launch_blue_t<LOGM, true, 0, 4>(a, st) : launch_blue_t<LOGM, false, 0, 4>(a, st);
         case 1: return launch_blue_t<LOGM, false, 1, 4>(a, st);
