@@ -111,6 +111,31 @@ __global__ void __launch_bounds__(StftGeom<LOGM, TB>::THREADS, StftGeom<LOGM, TB
   const long long F = a.frames;
   float* __restrict__ yr = a.yr + b * (long long)nbins * F;
   float* __restrict__ yi = a.yi + b * (long long)nbins * F;
+  if (a.onesided) {
+    // bins k and M-k from one pair of loads: with T = W_N^k O_k, X_k = E_k + T and
+    // X_{M-k} = conj(E_k - T) (W_N^{M-k} = -conj(W_N^k), E_{M-k} = conj(E_k), O_{M-k} = conj(O_k))
+    for (int idx = threadIdx.x; idx < (M / 2 + 1) * GM::G; idx += GM::THREADS) {
+      const int gg = idx % GM::G;
+      const int k = idx / GM::G;
+      const long long ff = f0 + gg;
+      if (ff >= F) continue;
+      const float2* fb = sm2 + gg * GM::FP;
+      const float2 z = fb[spad<S::SH>(k & (M - 1))];
+      const float2 v = fb[spad<S::SH>((M - k) & (M - 1))];
+      const float er = 0.5f * (z.x + v.x), ei = 0.5f * (z.y - v.y);
+      const float orr = 0.5f * (z.y + v.y), oi = 0.5f * (v.x - z.x);
+      const float2 tw = tw_lookup(k << (kTwLog - LOGN));
+      const float tr = orr * tw.x - oi * tw.y;
+      const float ti = orr * tw.y + oi * tw.x;
+      yr[(long long)k * F + ff] = (er + tr) * a.scale;
+      yi[(long long)k * F + ff] = (ei + ti) * a.scale;
+      if (2 * k != M) {
+        yr[(long long)(M - k) * F + ff] = (er - tr) * a.scale;
+        yi[(long long)(M - k) * F + ff] = (ti - ei) * a.scale;
+      }
+    }
+    return;
+  }
   for (int idx = threadIdx.x; idx < nbins * GM::G; idx += GM::THREADS) {
     const int gg = idx % GM::G;
     const int k = idx / GM::G;
