@@ -560,8 +560,10 @@ class LinearWL(Workload):
         self.name = f"ComplexLinear {K}->{N} on a {M}x{K} complex fp32 input, 3xTF32 tcgen05 (configs[1]b)"
         self.work = 8.0 * M * N * K
         self.dom_bytes = None
-        self.dominant = "k_gemm_tf32 (two launches of six TF32 segments each)"
+        self.dominant = "k_gemm_tf32 (three launches of three TF32 segments each: the three-product complex form)"
         self.bound = "tensor"
+        # tensor-core work actually issued: 3 real products x 3 TF32 segments x 2MNK
+        self.tensor_flops = 9 * 2.0 * M * N * K
 
     def setup(self, dev, g):
         import trnfft_b200 as trnfft
@@ -576,7 +578,7 @@ class LinearWL(Workload):
         torch.set_grad_enabled(False)
         self.step = lambda: self.layer(x)
         self.launches = {"linear": self.step}
-        self.launches_per_step = 4  # 2 split kernels (x; the weight split is cached) + 2 GEMMs
+        self.launches_per_step = 6  # 3 split kernels (x: real, imaginary, sum; the weight split is cached) + 3 GEMMs
         self.inputs = [self.xr, self.xi]
         self.e2e_fn = lambda ts: (lambda y: [y.real, y.imag])(self.layer(ComplexTensor(ts[0], ts[1])))
 
@@ -632,7 +634,7 @@ class SmallNGemm(SmallN):
 
         trnfft.set_small_n_algorithm("gemm")
         super().setup(dev, g)
-        self.tensor_flops = sum(3 * 8.0 * self.batch * n * n for n in (256,))
+        self.tensor_flops = sum(9 * 2.0 * self.batch * n * n for n in (256,))  # three-product form, 3xTF32
 
 
 class RealRoundTrip(Workload):

@@ -205,16 +205,19 @@ TRNFFT_API int trnfft_complex_mask_apply(const float* mask_re, const float* mask
                                          const float* spec_re, const float* spec_im, float* out_re, float* out_im,
                                          int64_t count, int device, void* stream);
 
-/* Work-area bytes trnfft_complex_linear needs: the TF32 hi/lo split of x and
- * W, 4*(M+N)*K floats.  -1 for negative sizes. */
+/* Work-area bytes trnfft_complex_linear needs: the TF32 hi/lo splits of the
+ * real part, the imaginary part and their sum, for x and for W:
+ * 6*(M+N)*K floats.  -1 for negative sizes. */
 TRNFFT_API int64_t trnfft_complex_linear_work_bytes(int64_t M, int64_t N, int64_t K);
 
 /* Complex linear map y = x W^T (+ b) on planar complex operands:
  * x (M x K), W (N x K, the nn.Linear weight layout), y (M x N), row-major,
  * b (N) optional (both parts or neither).  Replaces ComplexLinear.forward
  * (trnfft/nn.py:33-49) and trnfft.nki.dispatch.complex_linear
- * (trnfft/nki/dispatch.py:91-102): two tcgen05 TF32 tensor-core GEMMs with
- * the 3xTF32 split (hi*hi + hi*lo + lo*hi), float32 accuracy.  K must be a
+ * (trnfft/nki/dispatch.py:91-102): three tcgen05 TF32 tensor-core GEMMs in
+ * the three-product form P1 = Xr Wr^T, P2 = Xi Wi^T, P3 = (Xr+Xi)(Wr+Wi)^T,
+ * Re = P1 - P2, Im = P3 - P1 - P2, each with the 3xTF32 split
+ * (hi*hi + hi*lo + lo*hi), float32 accuracy.  K must be a
  * multiple of 4; all pointers 16-byte aligned; `work` holds
  * trnfft_complex_linear_work_bytes(M, N, K) bytes. */
 TRNFFT_API int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, const float* wi,
@@ -228,9 +231,15 @@ TRNFFT_API int trnfft_complex_linear(const float* xr, const float* xi, const flo
  * version), instead of re-splitting W on every forward. */
 TRNFFT_API int trnfft_split_tf32(const float* src, float* hi, float* lo, int64_t count, int device, void* stream);
 
-/* trnfft_complex_linear with W already split: w_split holds four N x K planes
- * in the order Wr_hi, Wr_lo, Wi_hi, Wi_lo (trnfft_split_tf32 of W_re and
- * W_im).  `work` holds the split of x: 4*M*K floats.  Replaces
+/* trnfft_split_tf32 of a + b (the sum rounded once to float32): the split of
+ * Wr + Wi that the third product of trnfft_complex_linear_presplit uses. */
+TRNFFT_API int trnfft_split_tf32_sum(const float* a, const float* b, float* hi, float* lo, int64_t count, int device,
+                                     void* stream);
+
+/* trnfft_complex_linear with W already split: w_split holds six N x K planes
+ * in the order Wr_hi, Wr_lo, Wi_hi, Wi_lo, Ws_hi, Ws_lo (trnfft_split_tf32 of
+ * W_re and W_im, trnfft_split_tf32_sum of the two).  `work` holds the split
+ * of x: 6*M*K floats.  Replaces
  * ComplexLinear.forward (trnfft/nn.py:33-49) for a weight that did not change
  * since it was split. */
 TRNFFT_API int trnfft_complex_linear_presplit(const float* xr, const float* xi, const float* w_split,

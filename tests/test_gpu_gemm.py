@@ -119,3 +119,40 @@ def test_complex_linear_on_a_second_device_after_the_first():
         got = torch.complex(y.real.double(), y.imag.double())
         assert y.real.device == torch.device(dev)
         assert float(torch.linalg.vector_norm(got - ref) / torch.linalg.vector_norm(ref)) < 1e-5
+
+
+_VARIANT_SCRIPT = r"""
+import numpy as np, torch
+import trnfft_b200 as trnfft
+from trnfft_b200 import ComplexTensor, _lib
+worst = 0.0
+for (M, N, K) in [(1, 7, 5), (300, 200, 128), (1000, 513, 260), (512, 768, 1024)]:
+    rng = np.random.default_rng(M + N + K)
+    x = (rng.standard_normal((M, K)) + 1j * rng.standard_normal((M, K))).astype(np.complex64)
+    w = ((rng.uniform(-1, 1, (N, K)) + 1j * rng.uniform(-1, 1, (N, K))) / np.sqrt(K)).astype(np.complex64)
+    b = (rng.standard_normal(N) + 1j * rng.standard_normal(N)).astype(np.complex64)
+    f = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    y = trnfft.nki.dispatch.complex_linear(ComplexTensor(f(x.real), f(x.imag)), f(w.real), f(w.imag), f(b.real), f(b.imag))
+    ref = x.astype(np.complex128) @ w.astype(np.complex128).T + b.astype(np.complex128)
+    got = y.real.double().cpu().numpy() + 1j * y.imag.double().cpu().numpy()
+    worst = max(worst, float(np.linalg.norm(got - ref) / np.linalg.norm(ref)))
+    assert _lib.device_status(torch.cuda.current_device()) == 0
+print("WORST", worst)
+"""
+
+
+@pytest.mark.parametrize("env", [{"TRNFFT_B200_GEMM_PAIR": "1"}, {"TRNFFT_B200_LINEAR_4M": "1"}],
+                         ids=["two-SM pair kernel", "four-product form"])
+def test_linear_variants_vs_fp64(env):
+    """The opt-in GEMM variants (selected once per process by environment variables, so each runs in
+    a child process) agree with fp64 like the default three-product one-CTA path."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _VARIANT_SCRIPT], cwd=root, env={**os.environ, **env},
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    worst = float(r.stdout.split("WORST")[-1])
+    assert worst < TOL

@@ -34,15 +34,18 @@ def _weight_key(wr, wi, k4):
 
 
 def split_weight(wr, wi, k4: int) -> torch.Tensor:
-    """The TF32 hi/lo split of a complex weight: one (4, N, k4) tensor holding
-    Wr_hi, Wr_lo, Wi_hi, Wi_lo (trnfft_split_tf32)."""
+    """The TF32 hi/lo split of a complex weight: one (6, N, k4) tensor holding
+    Wr_hi, Wr_lo, Wi_hi, Wi_lo, Ws_hi, Ws_lo with Ws = Wr + Wi (trnfft_split_tf32,
+    trnfft_split_tf32_sum), the operands of the three-product complex GEMM."""
     wr2, wi2 = (_aligned(_pad_k(t.float(), k4)) for t in (wr, wi))
     N = wr2.shape[0]
-    out = torch.empty(4, N, k4, dtype=torch.float32, device=wr2.device)
+    out = torch.empty(6, N, k4, dtype=torch.float32, device=wr2.device)
     dev = wr2.device.index if wr2.device.index is not None else torch.cuda.current_device()
+    st = _lib.stream_ptr(wr2.device)
     for i, t in enumerate((wr2, wi2)):
-        _lib.call("trnfft_split_tf32", _lib.ptr(t), _lib.ptr(out[2 * i]), _lib.ptr(out[2 * i + 1]), t.numel(), dev,
-                  _lib.stream_ptr(t.device))
+        _lib.call("trnfft_split_tf32", _lib.ptr(t), _lib.ptr(out[2 * i]), _lib.ptr(out[2 * i + 1]), t.numel(), dev, st)
+    _lib.call("trnfft_split_tf32_sum", _lib.ptr(wr2), _lib.ptr(wi2), _lib.ptr(out[4]), _lib.ptr(out[5]), wr2.numel(),
+              dev, st)
     return out
 
 
@@ -70,7 +73,7 @@ def linear_raw(xr, xi, wr, wi, br=None, bi=None, cache=None):
             cache["key"] = key
             cache["split"] = split_weight(wr, wi, k4)
         ws = cache["split"]
-        work = torch.empty(4 * M * k4, dtype=torch.float32, device=xr.device)
+        work = torch.empty(6 * M * k4, dtype=torch.float32, device=xr.device)
         _lib.call("trnfft_complex_linear_presplit", _lib.ptr(xr2), _lib.ptr(xi2), _lib.ptr(ws), _lib.ptr(br),
                   _lib.ptr(bi), _lib.ptr(yr), _lib.ptr(yi), M, N, k4, _lib.ptr(work), dev, _lib.stream_ptr(xr.device))
         return yr, yi

@@ -48,6 +48,7 @@ SIGNATURES = {
     "trnfft_complex_linear_work_bytes": (_I64, [_I64, _I64, _I64]),
     "trnfft_complex_linear": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _INT, _P]),
     "trnfft_split_tf32": (_INT, [_P, _P, _P, _I64, _INT, _P]),
+    "trnfft_split_tf32_sum": (_INT, [_P, _P, _P, _P, _I64, _INT, _P]),
     "trnfft_complex_linear_presplit": (_INT, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _P, _INT, _P]),
     "trnfft_exec_c2c_axis_tw": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _INT, _I64, _P]),
     "trnfft_ipc_handle_bytes": (_INT, []),

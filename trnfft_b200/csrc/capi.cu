@@ -976,13 +976,28 @@ int trnfft_exec_stft(trnfft_plan_t plan, const float* signal, int64_t batch, int
 
 int64_t trnfft_complex_linear_work_bytes(int64_t M, int64_t N, int64_t K) {
   if (M < 0 || N < 0 || K < 0) return -1;
-  return (int64_t)sizeof(float) * 4 * (M + N) * K;
+  return (int64_t)sizeof(float) * 6 * (M + N) * K;
 }
 
-// The two GEMMs of a complex linear map from split operands:
-// x_hi/lo (M x K, real then imaginary part), w_hi/lo (N x K, same order).
-static int complex_linear_gemms(float* const xs[4], const float* const ws[4], const float* br, const float* bi,
-                                float* yr, float* yi, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+// The complex linear map from split operands in the three-product form
+//   P1 = Xr Wr^T,  P2 = Xi Wi^T,  P3 = (Xr + Xi)(Wr + Wi)^T,
+//   Re = P1 - P2,  Im = P3 - P1 - P2,
+// three tcgen05 GEMMs of three TF32 segments each (hi*hi + hi*lo + lo*hi), 9 tensor-core products
+// instead of the 12 of the four-product form.  The first two GEMMs write P1 into yr and P2 into
+// yi; the third combines them in its epilogue (and adds the biases).
+// xs / ws: hi, lo of the real part, the imaginary part and their sum (six planes each).
+// TRNFFT_B200_LINEAR_4M=1 selects the four-product form (two GEMMs of six segments: Re = Xr Wr^T -
+// Xi Wi^T, Im = Xr Wi^T + Xi Wr^T), for measurement.
+static bool linear_four_products() {
+  static const bool v = [] {
+    const char* e = getenv("TRNFFT_B200_LINEAR_4M");
+    return e != nullptr && atoi(e) == 1;
+  }();
+  return v;
+}
+
+static int complex_linear_gemms4(float* const xs[6], const float* const ws[6], const float* br, const float* bi,
+                                 float* yr, float* yi, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
   GemmArgs ga;
   std::memset(&ga, 0, sizeof ga);
   for (int i = 0; i < 4; ++i) {
@@ -993,19 +1008,53 @@ static int complex_linear_gemms(float* const xs[4], const float* const ws[4], co
   ga.nb = 4;
   ga.M = M; ga.N = N; ga.K = K; ga.lda = K; ga.ldb = K; ga.ldc = N;
   ga.nseg = 6;
-  // real part: Xr Wr^T - Xi Wi^T, each product as hi*hi + hi*lo + lo*hi
   const int ra[6] = {0, 0, 1, 2, 2, 3}, rb[6] = {0, 1, 0, 2, 3, 2}, rn[6] = {0, 0, 0, 1, 1, 1};
   for (int i = 0; i < 6; ++i) { ga.seg_a[i] = ra[i]; ga.seg_b[i] = rb[i]; ga.seg_neg[i] = rn[i]; }
   ga.C = yr; ga.bias = br;
   cudaError_t e = launch_gemm_tf32(ga, st);
   if (e != cudaSuccess) return cuda_fail(e, "complex_linear: real part");
-  // imaginary part: Xr Wi^T + Xi Wr^T
   const int ia[6] = {0, 0, 1, 2, 2, 3}, ib[6] = {2, 3, 2, 0, 1, 0};
   for (int i = 0; i < 6; ++i) { ga.seg_a[i] = ia[i]; ga.seg_b[i] = ib[i]; ga.seg_neg[i] = 0; }
   ga.C = yi; ga.bias = bi;
   e = launch_gemm_tf32(ga, st);
   if (e != cudaSuccess) return cuda_fail(e, "complex_linear: imaginary part");
   return TRNFFT_SUCCESS;
+}
+
+static int complex_linear_gemms(float* const xs[6], const float* const ws[6], const float* br, const float* bi,
+                                float* yr, float* yi, int64_t M, int64_t N, int64_t K, cudaStream_t st) {
+  if (linear_four_products()) return complex_linear_gemms4(xs, ws, br, bi, yr, yi, M, N, K, st);
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof ga);
+  ga.na = 2;
+  ga.nb = 2;
+  ga.M = M; ga.N = N; ga.K = K; ga.lda = K; ga.ldb = K; ga.ldc = N;
+  ga.nseg = 3;
+  const int sa[3] = {0, 0, 1}, sb[3] = {0, 1, 0};
+  for (int i = 0; i < 3; ++i) { ga.seg_a[i] = sa[i]; ga.seg_b[i] = sb[i]; ga.seg_neg[i] = 0; }
+  static const char* what[3] = {"complex_linear: Xr Wr^T", "complex_linear: Xi Wi^T",
+                                "complex_linear: (Xr+Xi)(Wr+Wi)^T"};
+  for (int p = 0; p < 3; ++p) {
+    ga.A[0] = xs[2 * p]; ga.A[1] = xs[2 * p + 1];
+    ga.B[0] = ws[2 * p]; ga.B[1] = ws[2 * p + 1];
+    ga.C = p == 1 ? yi : yr;
+    ga.bias = p == 2 ? br : nullptr;
+    ga.epi = p == 2 ? 1 : 0;
+    ga.C2 = p == 2 ? yi : nullptr;
+    ga.bias2 = p == 2 ? bi : nullptr;
+    cudaError_t e = launch_gemm_tf32(ga, st);
+    if (e != cudaSuccess) return cuda_fail(e, what[p]);
+  }
+  return TRNFFT_SUCCESS;
+}
+
+// hi / lo of x's real part, imaginary part and their sum into xs[0..5]
+static cudaError_t split_complex(const float* xr, const float* xi, float* const xs[6], long long count,
+                                 cudaStream_t st) {
+  cudaError_t e = launch_split_tf32(xr, xs[0], xs[1], count, 1.f, st);
+  if (e == cudaSuccess) e = launch_split_tf32(xi, xs[2], xs[3], count, 1.f, st);
+  if (e == cudaSuccess) e = launch_split_tf32_sum(xr, xi, xs[4], xs[5], count, st);
+  return e;
 }
 
 int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, const float* wi, const float* br,
@@ -1022,14 +1071,16 @@ int trnfft_complex_linear(const float* xr, const float* xi, const float* wr, con
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   float* w = static_cast<float*>(work);
   const size_t mk = (size_t)M * K, nk = (size_t)N * K;
-  float* xs[4] = {w, w + mk, w + 2 * mk, w + 3 * mk};
-  float* wsp[4] = {w + 4 * mk, w + 4 * mk + nk, w + 4 * mk + 2 * nk, w + 4 * mk + 3 * nk};
-  cudaError_t e = launch_split_tf32(xr, xs[0], xs[1], (long long)mk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(xi, xs[2], xs[3], (long long)mk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(wr, wsp[0], wsp[1], (long long)nk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(wi, wsp[2], wsp[3], (long long)nk, 1.f, st);
+  float* xs[6];
+  float* wsp[6];
+  for (int i = 0; i < 6; ++i) {
+    xs[i] = w + i * mk;
+    wsp[i] = w + 6 * mk + i * nk;
+  }
+  cudaError_t e = split_complex(xr, xi, xs, (long long)mk, st);
+  if (e == cudaSuccess) e = split_complex(wr, wi, wsp, (long long)nk, st);
   if (e != cudaSuccess) return cuda_fail(e, "complex_linear: split");
-  const float* ws[4] = {wsp[0], wsp[1], wsp[2], wsp[3]};
+  const float* ws[6] = {wsp[0], wsp[1], wsp[2], wsp[3], wsp[4], wsp[5]};
   return complex_linear_gemms(xs, ws, br, bi, yr, yi, M, N, K, st);
 }
 
@@ -1042,6 +1093,19 @@ int trnfft_split_tf32(const float* src, float* hi, float* lo, int64_t count, int
   if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "split_tf32: cannot select device %d", device);
   cudaError_t e = launch_split_tf32(src, hi, lo, (long long)count, 1.f, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "split_tf32");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_split_tf32_sum(const float* a, const float* b, float* hi, float* lo, int64_t count, int device,
+                          void* stream) {
+  if (count < 0) return fail(TRNFFT_INVALID_VALUE, "split_tf32_sum: negative count");
+  if (count == 0) return TRNFFT_SUCCESS;
+  int rc = check_ptrs("split_tf32_sum", {a, b, hi, lo}, 16);
+  if (rc) return rc;
+  DeviceGuard g(device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "split_tf32_sum: cannot select device %d", device);
+  cudaError_t e = launch_split_tf32_sum(a, b, hi, lo, (long long)count, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "split_tf32_sum");
   return TRNFFT_SUCCESS;
 }
 
@@ -1060,11 +1124,14 @@ int trnfft_complex_linear_presplit(const float* xr, const float* xi, const float
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   float* w = static_cast<float*>(work);
   const size_t mk = (size_t)M * K, nk = (size_t)N * K;
-  float* xs[4] = {w, w + mk, w + 2 * mk, w + 3 * mk};
-  cudaError_t e = launch_split_tf32(xr, xs[0], xs[1], (long long)mk, 1.f, st);
-  if (e == cudaSuccess) e = launch_split_tf32(xi, xs[2], xs[3], (long long)mk, 1.f, st);
+  float* xs[6];
+  const float* ws[6];
+  for (int i = 0; i < 6; ++i) {
+    xs[i] = w + i * mk;
+    ws[i] = w_split + i * nk;
+  }
+  cudaError_t e = split_complex(xr, xi, xs, (long long)mk, st);
   if (e != cudaSuccess) return cuda_fail(e, "complex_linear_presplit: split");
-  const float* ws[4] = {w_split, w_split + nk, w_split + 2 * nk, w_split + 3 * nk};
   return complex_linear_gemms(xs, ws, br, bi, yr, yi, M, N, K, st);
 }
 

@@ -192,10 +192,17 @@ struct GemmArgs {
   float* C;
   const float* bias;
   long long M, N, K, lda, ldb, ldc;
+  // epi = 0: C = acc (+ bias).  epi = 1 (three-product complex form): C holds P1 and C2 holds
+  // P2 on entry; the epilogue writes C = P1 - P2 (+ bias) and C2 = acc - P1 - P2 (+ bias2).
+  int epi;
+  float* C2;
+  const float* bias2;
 };
 
 cudaError_t launch_gemm_tf32(const GemmArgs& g, cudaStream_t st);
 cudaError_t launch_split_tf32(const float* x, float* hi, float* lo, long long n, float scale, cudaStream_t st);
+// hi / lo of x + y (the operands of the third product of the three-product complex form)
+cudaError_t launch_split_tf32_sum(const float* x, const float* y, float* hi, float* lo, long long n, cudaStream_t st);
 
 // Multi-pass Bluestein helpers (bluestein_large.cu).
 cudaError_t launch_blue_pre(const float* xr, const float* xi, const float2* chirp, float* ar, float* ai,
