@@ -16,23 +16,26 @@
 // spectrum columns ([bins][G]; the G frames are contiguous in the (freq, time)
 // layout, so every load is a run of G floats), runs G real inverse transforms
 // on chip (an n_fft/2-point complex FFT of Z_k = E_k + i O_k, the packing of
-// the forward real kernels), and adds each frame's samples - windowed, raw,
-// and the squared window - into three segment accumulators in shared memory.
-// Each thread owns a fixed residue class of the segment's samples, so frames
-// add into a sample in frame order, like the reference's loop, without
-// atomics.  Every output sample is written exactly once; the H frames shared
-// with the previous segment are transformed twice (for n_fft = 2 hop, one in
-// G = 8).
+// the forward real kernels), and overlap-adds: each thread owns a fixed
+// residue class of the segment's samples and sums, in registers and in frame
+// order like the reference's loop, the windowed value, the raw value and the
+// squared window of the frames that cover each of its samples.  When P + H
+// frames fit in one chunk (n_fft = 2 hop: 8 frames for 7 frame starts) the
+// block normalises and writes its samples at once; otherwise the sums go into
+// three segment accumulators in shared memory once per chunk.  Every output
+// sample is written exactly once, without atomics.
+#include <cstdlib>
+
 #include "fft_common.cuh"
 #include "kernels.h"
 
 namespace tfb {
 
-template <int LOGM>
+template <int LOGM, int TB = 128>
 struct IstftGeom {
   static constexpr int LE = 4;
   using S = Sched<LOGM, LE>;
-  static constexpr int G0 = 128 / S::T;
+  static constexpr int G0 = TB / S::T;
   static constexpr int G = G0 < 1 ? 1 : G0;  // frames per chunk
   static constexpr int THREADS = G * S::T;  // every thread owns a slice of one frame
   static constexpr int M = S::N;
@@ -44,7 +47,8 @@ struct IstftGeom {
   static constexpr size_t frame_bytes = (size_t)G * FP * sizeof(float2);
   // ... followed by the segment accumulators (3 x SEG floats), sized at launch
   static constexpr size_t fixed_smem = ((tile_bytes > frame_bytes ? tile_bytes : frame_bytes) + 15) / 16 * 16;
-  static constexpr int MINB = 5;
+  // resident blocks per SM: up to 8, and 1024 threads' worth in all (64 registers per thread)
+  static constexpr int MINB = THREADS >= 1024 ? 1 : (1024 / THREADS < 8 ? 1024 / THREADS : 8);
 };
 
 // 4-byte asynchronous global -> shared copy; src_bytes = 0 fills zero
@@ -54,9 +58,9 @@ __device__ __forceinline__ void cp_async4(float* smem, const float* gmem, int sr
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
-template <int LOGM>
-__global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS, IstftGeom<LOGM>::MINB) k_istft(IstftArgs a) {
-  using GM = IstftGeom<LOGM>;
+template <int LOGM, int TB>
+__global__ void __launch_bounds__(IstftGeom<LOGM, TB>::THREADS, IstftGeom<LOGM, TB>::MINB) k_istft(IstftArgs a) {
+  using GM = IstftGeom<LOGM, TB>;
   using S = typename GM::S;
   constexpr int M = S::N;
   constexpr int N = 2 * M;
@@ -84,15 +88,28 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS, IstftGeom<LOGM>::MIN
   const float* __restrict__ xi = a.xi + b * (long long)nbins * F;
   const float* __restrict__ w = a.window;
 
-  for (int i = tid; i < a.seg; i += GM::THREADS) {
-    acc_w[i] = 0.f;
-    acc_r[i] = 0.f;
-    acc_e[i] = 0.f;
-  }
   // frames f with [f hop, f hop + N) meeting [t0, t1)
   const int flo = t0 - N + 1 <= 0 ? 0 : (t0 - N + hop) / hop;
   int fhi = (t1 - 1) / hop;
   if (fhi > F - 1) fhi = F - 1;
+  if (flo > fhi) {
+    // no frame reaches these samples (a requested length past the frames): zeros
+    for (int t = t0 + tid; t < t1; t += GM::THREADS) {
+      const long long o = (long long)t - a.pad_front;
+      if (o >= 0 && o < a.out_len) a.y[b * a.out_len + o] = 0.f;
+    }
+    return;
+  }
+  // one chunk covers all the block's frames: no segment accumulators (see the overlap-add);
+  // the launcher allocates them only when its geometry can give a block more than one chunk
+  const bool single = fhi - flo < G;
+  if (!single) {
+    for (int i = tid; i < a.seg; i += GM::THREADS) {
+      acc_w[i] = 0.f;
+      acc_r[i] = 0.f;
+      acc_e[i] = 0.f;
+    }
+  }
 
   for (int fc = flo; fc <= fhi; fc += G) {
     // stage the chunk's spectrum: tile[k][gg], k in [0, M]; the G frames of a bin are
@@ -149,29 +166,45 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS, IstftGeom<LOGM>::MIN
     }
     __syncthreads();
     smem_passes<LOGM, GM::LE, true, 1, S::P>(j, frames + g * GM::FP);
-    // overlap-add, frame by frame.  Thread tid owns the samples t = t0 + tid (mod THREADS),
-    // so the frames of the chunk add into each sample in frame order (as the reference's
-    // loop does) with no two threads touching one sample.
+    __syncthreads();
+    // overlap-add.  Thread tid owns the samples t = t0 + tid (mod THREADS) and sums, in frame
+    // order as the reference's loop does, the chunk's frames that cover t (at most
+    // ceil(n_fft / hop) of them) in registers: windowed, raw and squared window.  A block whose
+    // frames fit in one chunk normalises and writes its samples right away; otherwise the sums
+    // go into the segment accumulators once per chunk.
     const int fe = fc + G - 1 < fhi ? fc + G - 1 : fhi;
-    for (int f = fc; f <= fe; ++f) {
-      const int fs = f * hop;
-      const int lo = fs > t0 ? fs : t0;
-      const int hi = fs + N < t1 ? fs + N : t1;
-      // first owned sample >= lo
-      int t = lo + ((t0 + tid - lo) % GM::THREADS + GM::THREADS) % GM::THREADS;
-      const float2* fr = frames + (f - fc) * GM::FP;
-      for (; t < hi; t += GM::THREADS) {
-        const int off = t - fs;
-        const float2 z = fr[spad<S::SH>(off >> 1)];
+    for (int t = t0 + tid; t < t1; t += GM::THREADS) {
+      // frames f with f hop <= t < f hop + N, within [fc, fe]
+      int fa = t < N ? 0 : (t - N) / hop + 1;
+      int fb = t / hop;
+      if (fa < fc) fa = fc;
+      if (fb > fe) fb = fe;
+      float sw = 0.f, sr = 0.f, se = 0.f;
+      for (int f = fa; f <= fb; ++f) {
+        const int off = t - f * hop;
+        const float2 z = frames[(f - fc) * GM::FP + spad<S::SH>(off >> 1)];
         const float v = ((off & 1) ? z.y : z.x) * a.scale;
         const float ww = __ldg(w + off);
-        acc_w[t - t0] = fmaf(v, ww, acc_w[t - t0]);
-        acc_r[t - t0] += v;
-        acc_e[t - t0] = fmaf(ww, ww, acc_e[t - t0]);
+        sw = fmaf(v, ww, sw);
+        sr += v;
+        se = fmaf(ww, ww, se);
+      }
+      if (single) {
+        const long long o = (long long)t - a.pad_front;
+        if (o >= 0 && o < a.out_len) {
+          float out = 0.f;
+          if (t < a.exp_len) out = se > 1e-8f ? sw / se : sr;
+          a.y[b * a.out_len + o] = out;
+        }
+      } else if (fa <= fb) {
+        acc_w[t - t0] += sw;
+        acc_r[t - t0] += sr;
+        acc_e[t - t0] += se;
       }
     }
     __syncthreads();
   }
+  if (single) return;  // written above
 
   // normalisation, centre trim and length
   float* __restrict__ y = a.y + b * a.out_len;
@@ -187,9 +220,9 @@ __global__ void __launch_bounds__(IstftGeom<LOGM>::THREADS, IstftGeom<LOGM>::MIN
   }
 }
 
-template <int LOGM>
-static cudaError_t launch_istft_t(IstftArgs a, cudaStream_t st) {
-  using GM = IstftGeom<LOGM>;
+template <int LOGM, int TB>
+static cudaError_t launch_istft_tb(IstftArgs a, cudaStream_t st) {
+  using GM = IstftGeom<LOGM, TB>;
   constexpr int N = 2 * GM::M;
   // A block owns P consecutive frame starts (its segment is P * hop samples) and needs the
   // H = ceil(N / hop) - 1 frames before them: P + H = K * G frames, K whole chunks.
@@ -198,16 +231,17 @@ static cudaError_t launch_istft_t(IstftArgs a, cudaStream_t st) {
   if (K < 1) K = 1;
   long long P = K * GM::G - H;
   long long seg = P * a.hop;
-  // keep the three segment accumulators within 96 KB
-  while (seg * 12 > 96 * 1024 && P > 1) {
+  // with one chunk (K = 1) every block's frames fit in it and the overlap-add needs no segment
+  // accumulators; otherwise keep the three accumulators within 96 KB
+  while (K > 1 && seg * 12 > 96 * 1024 && P > 1) {
     --P;
     seg = P * a.hop;
   }
-  if (seg * 12 > 96 * 1024) return cudaErrorInvalidValue;  // hop beyond 8192 samples
+  if (seg > (1 << 30) || (K > 1 && seg * 12 > 96 * 1024)) return cudaErrorInvalidValue;  // hop beyond 8192
   a.seg = (int)seg;
   a.nseg = (a.total + seg - 1) / seg;
-  const size_t smem = GM::fixed_smem + 3 * (size_t)seg * sizeof(float);
-  auto kern = k_istft<LOGM>;
+  const size_t smem = GM::fixed_smem + (K > 1 ? 3 * (size_t)seg * sizeof(float) : 0);
+  auto kern = k_istft<LOGM, TB>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -217,6 +251,26 @@ static cudaError_t launch_istft_t(IstftArgs a, cudaStream_t st) {
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   kern<<<(unsigned)blocks, GM::THREADS, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+// TRNFFT_B200_ISTFT_THREADS (128, 256 or 512) sets the frames per chunk (threads / (n_fft/32)),
+// for measurement; 128 by default.
+static int istft_block_threads() {
+  static const int v = [] {
+    const char* e = getenv("TRNFFT_B200_ISTFT_THREADS");
+    const int t = e ? atoi(e) : 128;
+    return (t == 256 || t == 512) ? t : 128;
+  }();
+  return v;
+}
+
+template <int LOGM>
+static cudaError_t launch_istft_t(const IstftArgs& a, cudaStream_t st) {
+  switch (istft_block_threads()) {
+    case 256: return launch_istft_tb<LOGM, 256>(a, st);
+    case 512: return launch_istft_tb<LOGM, 512>(a, st);
+    default: return launch_istft_tb<LOGM, 128>(a, st);
+  }
 }
 
 cudaError_t launch_istft(int logn, const IstftArgs& a, cudaStream_t st) {
