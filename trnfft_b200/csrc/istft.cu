@@ -42,7 +42,12 @@ struct IstftGeom {
   static constexpr int FP = S::NP + ((2 - S::NP % 16) + 16) % 16;  // frame pitch (float2)
   // the spectrum tile (2 planes of (M+1) x G floats) shares its space with the frames
   // (float2): it is read into registers before the first pass writes the frames
-  static constexpr int TP = G + 1;  // tile floats per bin: an odd pitch keeps the C2R loads conflict-free
+  // tile floats per bin.  In the C2R pre-processing a warp reads bins k = j + T r of its
+  // FW = 32 / T frames (lanes: FW frames x T consecutive j): a pitch of FW x (odd) puts the
+  // warp's 32 loads in 32 distinct banks
+  static constexpr int FW = S::T < 32 ? 32 / S::T : 1;
+  static constexpr int TPO = (G + FW - 1) / FW;
+  static constexpr int TP = FW * (TPO % 2 ? TPO : TPO + 1);
   static constexpr size_t tile_bytes = 2 * (size_t)(M + 1) * TP * sizeof(float);
   static constexpr size_t frame_bytes = (size_t)G * FP * sizeof(float2);
   // ... followed by the segment accumulators (3 x SEG floats), sized at launch
