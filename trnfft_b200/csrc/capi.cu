@@ -568,6 +568,14 @@ static cudaError_t run_f64(const trnfft_plan_s* p, const double* xr, const doubl
     return run_f64_pow2(p, xr, xi, yr, yi, batch, inv, sc, work, st);
   // Bluestein: chirp premultiply, m-point FFT, times H, unscaled inverse m-point FFT (1/m is in H), postmultiply
   const long long m = p->m;
+  if (p->sub64 && p->sub64->logn <= kMaxF64BlueFusedLog) {
+    // the whole chain in one kernel (the padded transforms stay in shared memory)
+    F64BlueArgs fa;
+    fa.xr = xr; fa.xi = xi; fa.yr = yr; fa.yi = yi;
+    fa.chirp = p->chirp64; fa.H = p->H64;
+    fa.batch = batch; fa.n = (int)p->n; fa.scale = sc;
+    return launch_f64_blue_fused(p->sub64->logn, inv, fa, st);
+  }
   double* ar = work;
   double* ai = work + (size_t)m * batch;
   double* sub_work = work + 2 * (size_t)m * batch;

@@ -21,6 +21,8 @@
 // Twiddles inside a block come from a per-device table W_4096^i in double.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "kernels.h"
 
 namespace tfb {
@@ -286,6 +288,254 @@ cudaError_t launch_f64_blue_post(const double* ar, const double* ai, const doubl
                                  long long batch, long long n, long long m, bool inv, double scale, cudaStream_t st) {
   k_f64_blue_post<<<ew_blocks(batch * n), 256, 0, st>>>(ar, ai, chirp, yr, yi, batch, n, m, inv ? 1 : 0, scale);
   return cudaGetLastError();
+}
+
+// ---- fused Bluestein (m <= 8192) -------------------------------------------
+// The chain above makes five (m <= 4096) or seven (m = 8192) passes over the padded batch in
+// HBM; here one block holds whole padded transforms in shared memory and does every stage:
+// x read once, y written once.  m <= 4096: F64Geom's C transforms per 256-thread block and the
+// radix-4 block FFT.  m = 8192 (128 KB of double2, one transform per block): radix-2 Stockham
+// passes with 512 threads, each holding 8 butterflies (a radix-4 pass would hold 16 double2 per
+// thread, more registers than a 512-thread block has); the last pass's twiddles W_8192^k are
+// W_4096^(k/2), times W_8192 for odd k.
+
+constexpr int kF64BigThreads = 512;
+
+// m = 8192 with 1024 threads: six radix-4 passes (2 butterflies of 4 values per thread) and a
+// final radix-2 pass (4 butterflies per thread), half the shared-memory traffic of radix 2
+constexpr int kF64Big4Threads = 1024;
+
+template <int LOGL, bool INV>
+__device__ __forceinline__ void f64_fft_r4_big(double2* sb, double2 w_half) {
+  constexpr int NT = kF64Big4Threads;
+  constexpr int L = 1 << LOGL;
+  constexpr int BPT4 = L / 4 / NT;
+  constexpr int BPT2 = L / 2 / NT;
+  static_assert(BPT4 >= 1 && (LOGL & 1) && LOGL == kTw64Log + 1, "radix-4 block FFT geometry (m = 8192)");
+#pragma unroll 1
+  for (int lns = 0; lns + 2 <= LOGL; lns += 2) {
+    const int ns = 1 << lns;
+    double2 v[BPT4][4];
+#pragma unroll
+    for (int q = 0; q < BPT4; ++q) {
+      const int j = threadIdx.x + q * NT;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) v[q][r] = sb[j + r * (L / 4)];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < BPT4; ++q) {
+      const int j = threadIdx.x + q * NT;
+      const int k = j & (ns - 1);
+      double2 a0 = v[q][0], a1 = v[q][1], a2 = v[q][2], a3 = v[q][3];
+      if (ns > 1) {
+        const int step = k << (kTw64Log - lns - 2);  // W_{4 ns}^k = W_4096^(k 4096 / (4 ns)), lns <= 10
+        a1 = cmul64(a1, tw64<INV>(step));
+        a2 = cmul64(a2, tw64<INV>(2 * step));
+        a3 = cmul64(a3, tw64<INV>(3 * step));
+      }
+      const double2 s02 = make_double2(a0.x + a2.x, a0.y + a2.y), d02 = make_double2(a0.x - a2.x, a0.y - a2.y);
+      const double2 s13 = make_double2(a1.x + a3.x, a1.y + a3.y), d13 = make_double2(a1.x - a3.x, a1.y - a3.y);
+      const double2 md13 = INV ? make_double2(-d13.y, d13.x) : make_double2(d13.y, -d13.x);
+      const int base = ((j >> lns) << (lns + 2)) + k;
+      sb[base] = make_double2(s02.x + s13.x, s02.y + s13.y);
+      sb[base + ns] = make_double2(d02.x + md13.x, d02.y + md13.y);
+      sb[base + 2 * ns] = make_double2(s02.x - s13.x, s02.y - s13.y);
+      sb[base + 3 * ns] = make_double2(d02.x - md13.x, d02.y - md13.y);
+    }
+    __syncthreads();
+  }
+  {
+    constexpr int lns = LOGL - 1;  // 12: W_8192^k = W_4096^(k/2) (x W_8192 for odd k)
+    constexpr int ns = 1 << lns;
+    double2 v[BPT2][2];
+#pragma unroll
+    for (int q = 0; q < BPT2; ++q) {
+      const int j = threadIdx.x + q * NT;
+      v[q][0] = sb[j];
+      v[q][1] = sb[j + L / 2];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < BPT2; ++q) {
+      const int j = threadIdx.x + q * NT;
+      const int k = j & (ns - 1);
+      double2 w = tw64<INV>(k >> 1);
+      if (k & 1) w = cmul64(w, w_half);
+      const double2 a0 = v[q][0], a1 = cmul64(v[q][1], w);
+      const int base = ((j >> lns) << (lns + 1)) + k;
+      sb[base] = make_double2(a0.x + a1.x, a0.y + a1.y);
+      sb[base + ns] = make_double2(a0.x - a1.x, a0.y - a1.y);
+    }
+    __syncthreads();
+  }
+}
+
+template <int LOGL, bool INV>
+__device__ __forceinline__ void f64_fft_r2_big(double2* sb, double2 w_half) {
+  constexpr int L = 1 << LOGL;
+  constexpr int NB = L / 2;
+  constexpr int BPT = NB / kF64BigThreads;
+  static_assert(NB % kF64BigThreads == 0 && LOGL <= kTw64Log + 1, "radix-2 block FFT geometry");
+#pragma unroll 1
+  for (int lns = 0; lns < LOGL; ++lns) {
+    const int ns = 1 << lns;
+    double2 v[BPT][2];
+#pragma unroll
+    for (int q = 0; q < BPT; ++q) {
+      const int j = threadIdx.x + q * kF64BigThreads;
+      v[q][0] = sb[j];
+      v[q][1] = sb[j + NB];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < BPT; ++q) {
+      const int j = threadIdx.x + q * kF64BigThreads;
+      const int k = j & (ns - 1);
+      double2 a0 = v[q][0], a1 = v[q][1];
+      if (lns > 0) {
+        double2 w;
+        if (lns + 1 <= kTw64Log) {
+          w = tw64<INV>(k << (kTw64Log - lns - 1));  // W_{2 ns}^k
+        } else {
+          w = tw64<INV>(k >> 1);  // W_{2 ns}^k with 2 ns = 2 * 4096
+          if (k & 1) w = cmul64(w, w_half);
+        }
+        a1 = cmul64(a1, w);
+      }
+      const int base = ((j >> lns) << (lns + 1)) + k;
+      sb[base] = make_double2(a0.x + a1.x, a0.y + a1.y);
+      sb[base + ns] = make_double2(a0.x - a1.x, a0.y - a1.y);
+    }
+    __syncthreads();
+  }
+}
+
+__device__ __forceinline__ double2 blue_chirp(const double2* chirp, int j, bool inv) {
+  double2 c = chirp[j];
+  if (inv) c.y = -c.y;
+  return c;
+}
+__device__ __forceinline__ double2 blue_h(const double2* H, int k, int m, bool inv) {
+  double2 h = H[inv ? ((m - k) & (m - 1)) : k];
+  if (inv) h.y = -h.y;
+  return h;
+}
+
+// m <= 4096: C transforms per block (sequence c of the block is row blockIdx.x * C + c)
+template <int LOGM, bool INV>
+__global__ void __launch_bounds__(kF64Threads) k_f64_blue_small(F64BlueArgs a) {
+  using GM = F64Geom<LOGM>;
+  constexpr int M = GM::L;
+  constexpr int C = GM::C;
+  extern __shared__ double2 sb[];
+  const long long r0 = (long long)blockIdx.x * C;
+  const int n = a.n;
+  for (int idx = threadIdx.x; idx < C * M; idx += kF64Threads) {
+    const int c = idx / M, j = idx % M;
+    const long long r = r0 + c;
+    double2 v = make_double2(0.0, 0.0);
+    if (j < n && r < a.batch)
+      v = cmul64(make_double2(a.xr[r * n + j], a.xi[r * n + j]), blue_chirp(a.chirp, j, INV));
+    sb[idx] = v;
+  }
+  __syncthreads();
+  f64_block_fft<LOGM, false>(sb);
+  for (int idx = threadIdx.x; idx < C * M; idx += kF64Threads) sb[idx] = cmul64(sb[idx], blue_h(a.H, idx % M, M, INV));
+  __syncthreads();
+  f64_block_fft<LOGM, true>(sb);  // unscaled: 1/m is folded into H
+  for (int idx = threadIdx.x; idx < C * n; idx += kF64Threads) {
+    const int c = idx / n, j = idx % n;
+    const long long r = r0 + c;
+    if (r >= a.batch) break;
+    const double2 v = cmul64(sb[c * M + j], blue_chirp(a.chirp, j, INV));
+    a.yr[r * n + j] = v.x * a.scale;
+    a.yi[r * n + j] = v.y * a.scale;
+  }
+}
+
+// m = 8192: one transform per block; R4 selects the 1024-thread radix-4 block FFT
+template <bool INV, bool R4>
+__global__ void __launch_bounds__(R4 ? kF64Big4Threads : kF64BigThreads, 1) k_f64_blue_big(F64BlueArgs a) {
+  constexpr int LOGM = 13;
+  constexpr int M = 1 << LOGM;
+  constexpr int NT = R4 ? kF64Big4Threads : kF64BigThreads;
+  extern __shared__ double2 sb[];
+  const long long r = blockIdx.x;
+  const int n = a.n;
+  double s, c;
+  sincospi(2.0 / M, &s, &c);  // W_M = exp(-2 pi i / M)
+  for (int j = threadIdx.x; j < M; j += NT) {
+    double2 v = make_double2(0.0, 0.0);
+    if (j < n) v = cmul64(make_double2(a.xr[r * n + j], a.xi[r * n + j]), blue_chirp(a.chirp, j, INV));
+    sb[j] = v;
+  }
+  __syncthreads();
+  if constexpr (R4) f64_fft_r4_big<LOGM, false>(sb, make_double2(c, -s));
+  else f64_fft_r2_big<LOGM, false>(sb, make_double2(c, -s));
+  for (int k = threadIdx.x; k < M; k += NT) sb[k] = cmul64(sb[k], blue_h(a.H, k, M, INV));
+  __syncthreads();
+  // unscaled inverse: 1/m is folded into H
+  if constexpr (R4) f64_fft_r4_big<LOGM, true>(sb, make_double2(c, s));
+  else f64_fft_r2_big<LOGM, true>(sb, make_double2(c, s));
+  for (int j = threadIdx.x; j < n; j += NT) {
+    const double2 v = cmul64(sb[j], blue_chirp(a.chirp, j, INV));
+    a.yr[r * n + j] = v.x * a.scale;
+    a.yi[r * n + j] = v.y * a.scale;
+  }
+}
+
+// TRNFFT_B200_F64_BLUE_R2=1 selects the 512-thread radix-2 variant of the m = 8192 kernel.
+static bool f64_blue_r2() {
+  static const bool v = [] {
+    const char* e = getenv("TRNFFT_B200_F64_BLUE_R2");
+    return e != nullptr && atoi(e) == 1;
+  }();
+  return v;
+}
+
+template <int LOGM>
+static cudaError_t launch_blue_small(bool inv, const F64BlueArgs& a, cudaStream_t st) {
+  using GM = F64Geom<LOGM>;
+  auto kern = inv ? k_f64_blue_small<LOGM, true> : k_f64_blue_small<LOGM, false>;
+  if (GM::smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GM::smem);
+    if (e != cudaSuccess) return e;
+  }
+  const long long blocks = (a.batch + GM::C - 1) / GM::C;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  kern<<<(unsigned)blocks, kF64Threads, GM::smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_f64_blue_fused(int logm, bool inv, const F64BlueArgs& a, cudaStream_t st) {
+  if (a.batch <= 0) return cudaSuccess;
+  switch (logm) {
+    case 1: return launch_blue_small<1>(inv, a, st);
+    case 2: return launch_blue_small<2>(inv, a, st);
+    case 3: return launch_blue_small<3>(inv, a, st);
+    case 4: return launch_blue_small<4>(inv, a, st);
+    case 5: return launch_blue_small<5>(inv, a, st);
+    case 6: return launch_blue_small<6>(inv, a, st);
+    case 7: return launch_blue_small<7>(inv, a, st);
+    case 8: return launch_blue_small<8>(inv, a, st);
+    case 9: return launch_blue_small<9>(inv, a, st);
+    case 10: return launch_blue_small<10>(inv, a, st);
+    case 11: return launch_blue_small<11>(inv, a, st);
+    case 12: return launch_blue_small<12>(inv, a, st);
+    case 13: {
+      const bool r2 = f64_blue_r2();
+      auto kern = r2 ? (inv ? k_f64_blue_big<true, false> : k_f64_blue_big<false, false>)
+                     : (inv ? k_f64_blue_big<true, true> : k_f64_blue_big<false, true>);
+      const size_t smem = sizeof(double2) << 13;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      if (a.batch > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+      kern<<<(unsigned)a.batch, r2 ? kF64BigThreads : kF64Big4Threads, smem, st>>>(a);
+      return cudaGetLastError();
+    }
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // float32 <-> float64 plane conversion (precision="double" on float32 tensors)

@@ -172,6 +172,22 @@ cudaError_t launch_f64_to_f32(const double* x, float* y, long long count, cudaSt
 // Upload W_4096^i in double to the current device (f64.cu), once per device.
 cudaError_t upload_tw64(const double2* host_table);
 
+// Fused fp64 Bluestein for padded lengths m = 2^logm <= 8192: chirp premultiply, m-point FFT,
+// times H, unscaled inverse m-point FFT, chirp postmultiply and scale in one kernel (f64.cu).
+struct F64BlueArgs {
+  const double* xr;
+  const double* xi;
+  double* yr;
+  double* yi;
+  const double2* chirp;
+  const double2* H;
+  long long batch;
+  int n;
+  double scale;
+};
+constexpr int kMaxF64BlueFusedLog = 13;
+cudaError_t launch_f64_blue_fused(int logm, bool inv, const F64BlueArgs& a, cudaStream_t st);
+
 // Element-wise complex product y = m[i mod mcount] * s[i] (mask.cu), i < count.
 cudaError_t launch_cmul(const float* mr, const float* mi, long long mcount, const float* sr, const float* si,
                         float* yr, float* yi, long long count, cudaStream_t st);
