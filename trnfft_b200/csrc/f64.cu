@@ -16,8 +16,10 @@
 // (two-level fp64 table) multiplies output k: that is the inter-pass twiddle
 // of the four-step split N = N1 * N2 used for N > 4096 (pass A over the
 // strided columns with the twiddle, pass B over the rows with a transposing
-// store, so the result is in natural order).  Bluestein sizes chain
-// elementwise chirp kernels around two such transforms of the padded length.
+// store, so the result is in natural order).  Bluestein sizes whose padded
+// length m is at most 8192 run as one fused kernel (k_f64_blue_small / _big:
+// the padded transforms stay in shared memory); longer ones chain elementwise
+// chirp kernels around two such transforms of the padded length.
 // Twiddles inside a block come from a per-device table W_4096^i in double.
 #include <cuda_runtime.h>
 
