@@ -140,9 +140,20 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
   constexpr int L = GM::L;
   constexpr int C = GM::C;
   extern __shared__ double2 sb[];
+  // per-sequence offsets, computed once per block (the 64-bit divisions stay out of the loops)
+  __shared__ long long s_in[C], s_out[C];
+  __shared__ unsigned long long s_tw[C];
   const long long s0 = (long long)blockIdx.x * C;
   int cn = C;
   if (s0 + cn > a.nseq) cn = (int)(a.nseq - s0);
+  if (threadIdx.x < cn) {
+    const long long s = s0 + threadIdx.x;
+    const long long q = s / a.inner, r = s - q * a.inner;
+    s_in[threadIdx.x] = q * a.in_outer + r * a.in_cs;
+    s_out[threadIdx.x] = q * a.out_outer + r * a.out_cs;
+    s_tw[threadIdx.x] = (unsigned long long)(r + a.tw_off);
+  }
+  __syncthreads();
   // load: walk the C x L tile along whichever axis is contiguous in memory
   const bool in_seq_fast = a.in_js != 1;  // neighbouring sequences adjacent: sequence index fastest
   for (int idx = threadIdx.x; idx < C * L; idx += kF64Threads) {
@@ -150,8 +161,7 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
     if (in_seq_fast) { c = idx % C; j = idx / C; } else { c = idx / L; j = idx % L; }
     double2 v = make_double2(0.0, 0.0);
     if (c < cn) {
-      const long long s = s0 + c;
-      const long long off = (s / a.inner) * a.in_outer + (s % a.inner) * a.in_cs + (long long)j * a.in_js;
+      const long long off = s_in[c] + (long long)j * a.in_js;
       v = make_double2(a.xr[off], a.xi[off]);
     }
     sb[c * L + j] = v;
@@ -163,16 +173,14 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
     int c, k;
     if (out_seq_fast) { c = idx % C; k = idx / C; } else { c = idx / L; k = idx % L; }
     if (c >= cn) continue;
-    const long long s = s0 + c;
     double2 v = sb[c * L + k];
     if (a.tw_hi) {
-      const unsigned long long e =
-          ((unsigned long long)((s % a.inner) + a.tw_off) * (unsigned long long)k) & a.tw_mask;
+      const unsigned long long e = (s_tw[c] * (unsigned long long)k) & a.tw_mask;
       double2 w = cmul64(a.tw_hi[e >> a.tw_split], a.tw_lo[e & ((1ULL << a.tw_split) - 1)]);
       if (INV) w.y = -w.y;
       v = cmul64(v, w);
     }
-    const long long off = (s / a.inner) * a.out_outer + (s % a.inner) * a.out_cs + (long long)k * a.out_ks;
+    const long long off = s_out[c] + (long long)k * a.out_ks;
     a.yr[off] = v.x * a.scale;
     a.yi[off] = v.y * a.scale;
   }
