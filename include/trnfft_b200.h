@@ -156,6 +156,15 @@ TRNFFT_API int trnfft_plan_query_f64(trnfft_plan_t plan, int64_t batch, int64_t*
 TRNFFT_API int trnfft_exec_c2c_f64(trnfft_plan_t plan, const double* in_re, const double* in_im, double* out_re,
                                    double* out_im, int64_t batch, int inverse, void* work, void* stream);
 
+/* trnfft_exec_c2c_f64 on planar float32 input and output: every stage runs in
+ * float64 (precision="double" on float32 tensors, trnfft/fft_core.py:1306-1309,
+ * 1372-1374 cast to float64 and back); the widening happens in the first
+ * kernel's loads and the narrowing in the last kernel's stores, so no float64
+ * copy of the data is made.  Pointers 4-byte aligned; the same work area as
+ * trnfft_exec_c2c_f64 (trnfft_plan_query_f64). */
+TRNFFT_API int trnfft_exec_c2c_f64_f32io(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out_re,
+                                         float* out_im, int64_t batch, int inverse, void* work, void* stream);
+
 /* Convert `count` values between float32 and float64 on `device` (to_double
  * != 0: float -> double).  Used to run float32 data through the fp64
  * transforms of precision="double" (the reference casts with .double() and

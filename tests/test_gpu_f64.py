@@ -98,3 +98,46 @@ def test_float64_fft2_matches_numpy():
     X = trnfft.fft2(ComplexTensor(_c64(x.real), _c64(x.imag)))
     got = X.real.cpu().numpy() + 1j * X.imag.cpu().numpy()
     assert rel_l2(got, np.fft.fft2(x)) < F64_TOL
+
+
+def test_convert_f32_f64_entry_point():
+    """trnfft_convert_f32_f64 widens and narrows exactly like a cast (round to nearest)."""
+    from trnfft_b200 import _lib
+
+    rng = np.random.default_rng(5)
+    x = torch.from_numpy(rng.standard_normal(10007).astype(np.float32)).cuda()
+    d = torch.empty(x.shape, dtype=torch.float64, device="cuda")
+    _lib.call("trnfft_convert_f32_f64", _lib.ptr(x), _lib.ptr(d), x.numel(), 1, 0, _lib.stream_ptr(x.device))
+    assert torch.equal(d, x.double())
+    d2 = torch.from_numpy(rng.standard_normal(10007)).cuda()
+    f = torch.empty(d2.shape, dtype=torch.float32, device="cuda")
+    _lib.call("trnfft_convert_f32_f64", _lib.ptr(d2), _lib.ptr(f), d2.numel(), 0, 0, _lib.stream_ptr(d2.device))
+    assert torch.equal(f, d2.float())
+
+
+@pytest.mark.parametrize("n", [1, 64, 4096, 1 << 15, 4093, 40961])
+def test_f32io_entry_matches_double_entry(n):
+    """trnfft_exec_c2c_f64_f32io (float32 planes in and out, fp64 inside) equals the float64 entry
+    on the widened input, rounded to float32, for one-pass, two-pass, fused-Bluestein and
+    chained-Bluestein plans."""
+    from trnfft_b200 import _lib
+
+    rng = np.random.default_rng(n)
+    B = 3
+    xr = torch.from_numpy(rng.standard_normal((B, n)).astype(np.float32)).cuda()
+    xi = torch.from_numpy(rng.standard_normal((B, n)).astype(np.float32)).cuda()
+    plan = _lib.device_plan(n, xr.device)
+    plan.enable_f64()
+    wb = plan.work_bytes_f64(B)
+    work = torch.empty(max(wb, 16), dtype=torch.uint8, device="cuda")
+    st = _lib.stream_ptr(xr.device)
+    for inv in (0, 1):
+        yr = torch.empty_like(xr)
+        yi = torch.empty_like(xi)
+        _lib.call("trnfft_exec_c2c_f64_f32io", plan.handle, _lib.ptr(xr), _lib.ptr(xi), _lib.ptr(yr), _lib.ptr(yi), B,
+                  inv, _lib.ptr(work), st)
+        ar, ai = xr.double(), xi.double()
+        dr, di = torch.empty_like(ar), torch.empty_like(ai)
+        _lib.call("trnfft_exec_c2c_f64", plan.handle, _lib.ptr(ar), _lib.ptr(ai), _lib.ptr(dr), _lib.ptr(di), B, inv,
+                  _lib.ptr(work), st)
+        assert torch.equal(yr, dr.float()) and torch.equal(yi, di.float())

@@ -63,6 +63,7 @@ SIGNATURES = {
     "trnfft_plan_enable_f64": (_INT, [_P]),
     "trnfft_plan_query_f64": (_INT, [_P, _I64, ctypes.POINTER(_I64)]),
     "trnfft_exec_c2c_f64": (_INT, [_P, _P, _P, _P, _P, _I64, _INT, _P, _P]),
+    "trnfft_exec_c2c_f64_f32io": (_INT, [_P, _P, _P, _P, _P, _I64, _INT, _P, _P]),
     "trnfft_convert_f32_f64": (_INT, [_P, _P, _I64, _INT, _INT, _P]),
     "trnfft_exec_istft": (_INT, [_P, _P, _P, _I64, _I64, _I64, _P, _INT, _INT, _INT, _I64, _P, _P]),
     "trnfft_complex_mask_apply": (_INT, [_P, _P, _I64, _P, _P, _P, _P, _I64, _INT, _P]),

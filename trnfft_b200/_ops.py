@@ -44,27 +44,18 @@ def _f64_wanted(t: torch.Tensor, precision=None) -> bool:
     return t.dtype == torch.float64 or _resolve(precision) == "double"
 
 
-def _convert(src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    """float32 <-> float64 copy on the library's conversion kernel."""
-    src = src.contiguous()
-    out = torch.empty(src.shape, dtype=dtype, device=src.device)
-    if src.numel():
-        _lib.call("trnfft_convert_f32_f64", _lib.ptr(src), _lib.ptr(out), src.numel(),
-                  int(dtype == torch.float64), src.device.index, _lib.stream_ptr(src.device))
-    return out
-
-
 def c2c_f64_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool):
     """Transform along the last axis with every stage in fp64 (trnfft_exec_c2c_f64).
-    float32 inputs are widened on the device and the result narrowed back."""
+    float32 inputs stay float32 in memory: trnfft_exec_c2c_f64_f32io widens them in the first
+    kernel's loads and narrows the result in the last kernel's stores."""
     _check(xr, "real part", True)
     _check(xi, "imaginary part", True)
     n = xr.shape[-1]
     shape, odt = xr.shape, xr.dtype
     a = _flat(xr, n)
     b = _flat(xi.to(odt), n)
-    if odt != torch.float64:
-        a, b = _convert(a, torch.float64), _convert(b, torch.float64)
+    if odt not in (torch.float32, torch.float64):
+        a, b = a.float(), b.float()
     batch = a.shape[0]
     yr = torch.empty_like(a)
     yi = torch.empty_like(b)
@@ -73,10 +64,11 @@ def c2c_f64_raw(xr: torch.Tensor, xi: torch.Tensor, inverse: bool):
         plan.enable_f64()
         wb = plan.work_bytes_f64(batch)
         work = torch.empty(wb, dtype=torch.uint8, device=a.device) if wb else None
-        _lib.call("trnfft_exec_c2c_f64", plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi), batch,
+        entry = "trnfft_exec_c2c_f64" if a.dtype == torch.float64 else "trnfft_exec_c2c_f64_f32io"
+        _lib.call(entry, plan.handle, _lib.ptr(a), _lib.ptr(b), _lib.ptr(yr), _lib.ptr(yi), batch,
                   int(bool(inverse)), _lib.ptr(work), _lib.stream_ptr(a.device))
-    if odt != torch.float64:
-        yr, yi = _convert(yr, odt), _convert(yi, odt)
+    if yr.dtype != odt:
+        yr, yi = yr.to(odt), yi.to(odt)
     return yr.reshape(shape), yi.reshape(shape)
 
 

@@ -513,9 +513,19 @@ static int64_t f64_work_bytes(const trnfft_plan_s* p, int64_t batch) {
   return 0;
 }
 
+// float32 input / output planes of an fp64 transform (converted in the first kernel's loads and
+// the last kernel's stores); null: the double planes are used
+struct F32IO {
+  const float* xr;
+  const float* xi;
+  float* yr;
+  float* yi;
+};
+
 // Power-of-two fp64 transform of `batch` contiguous rows; `scale` multiplies the result.
 static cudaError_t run_f64_pow2(const trnfft_plan_s* p, const double* xr, const double* xi, double* yr, double* yi,
-                                int64_t batch, bool inv, double scale, double* work, cudaStream_t st) {
+                                int64_t batch, bool inv, double scale, double* work, cudaStream_t st,
+                                const F32IO* io = nullptr) {
   const int L = p->logn;
   const long long N = p->n;
   F64SeqArgs a;
@@ -526,6 +536,7 @@ static cudaError_t run_f64_pow2(const trnfft_plan_s* p, const double* xr, const 
     a.in_outer = N; a.in_js = 1;
     a.out_outer = N; a.out_ks = 1;
     a.scale = scale;
+    if (io) { a.xr32 = io->xr; a.xi32 = io->xi; a.yr32 = io->yr; a.yi32 = io->yi; }
     return launch_f64_seq(L, inv, a, st);
   }
   // N = N1 * N2, n = n1 N2 + n2, k = k1 + N1 k2:
@@ -542,6 +553,7 @@ static cudaError_t run_f64_pow2(const trnfft_plan_s* p, const double* xr, const 
   a.tw_hi = p->tw64_hi; a.tw_lo = p->tw64_lo; a.tw_split = p->tw64_split;
   a.tw_mask = (unsigned long long)(N - 1); a.tw_off = 0;
   a.scale = 1.0;
+  if (io) { a.xr32 = io->xr; a.xi32 = io->xi; }
   cudaError_t e = launch_f64_seq(l1, inv, a, st);
   if (e != cudaSuccess) return e;
   F64SeqArgs b;
@@ -551,21 +563,26 @@ static cudaError_t run_f64_pow2(const trnfft_plan_s* p, const double* xr, const 
   b.in_outer = N; b.in_cs = N2; b.in_js = 1;
   b.out_outer = N; b.out_cs = 1; b.out_ks = N1;
   b.scale = scale;
+  if (io) { b.yr32 = io->yr; b.yi32 = io->yi; }
   return launch_f64_seq(l2, inv, b, st);
 }
 
 static cudaError_t run_f64(const trnfft_plan_s* p, const double* xr, const double* xi, double* yr, double* yi,
-                           int64_t batch, bool inv, double* work, cudaStream_t st) {
+                           int64_t batch, bool inv, double* work, cudaStream_t st, const F32IO* io = nullptr) {
   const double sc = inv ? 1.0 / (double)p->n : 1.0;
   if (p->algorithm == TRNFFT_ALG_COPY) {
-    const size_t bytes = sizeof(double) * (size_t)batch;
+    const void* sr = io ? (const void*)io->xr : (const void*)xr;
+    const void* si = io ? (const void*)io->xi : (const void*)xi;
+    void* dr = io ? (void*)io->yr : (void*)yr;
+    void* di = io ? (void*)io->yi : (void*)yi;
+    const size_t bytes = (io ? sizeof(float) : sizeof(double)) * (size_t)batch;
     cudaError_t e = cudaSuccess;
-    if (yr != xr) e = cudaMemcpyAsync(yr, xr, bytes, cudaMemcpyDeviceToDevice, st);
-    if (e == cudaSuccess && yi != xi) e = cudaMemcpyAsync(yi, xi, bytes, cudaMemcpyDeviceToDevice, st);
+    if (dr != sr) e = cudaMemcpyAsync(dr, sr, bytes, cudaMemcpyDeviceToDevice, st);
+    if (e == cudaSuccess && di != si) e = cudaMemcpyAsync(di, si, bytes, cudaMemcpyDeviceToDevice, st);
     return e;
   }
   if (p->algorithm != TRNFFT_ALG_BLUESTEIN && p->algorithm != TRNFFT_ALG_MIXED)
-    return run_f64_pow2(p, xr, xi, yr, yi, batch, inv, sc, work, st);
+    return run_f64_pow2(p, xr, xi, yr, yi, batch, inv, sc, work, st, io);
   // Bluestein: chirp premultiply, m-point FFT, times H, unscaled inverse m-point FFT (1/m is in H), postmultiply
   const long long m = p->m;
   if (p->sub64 && p->sub64->logn <= kMaxF64BlueFusedLog) {
@@ -574,16 +591,21 @@ static cudaError_t run_f64(const trnfft_plan_s* p, const double* xr, const doubl
     fa.xr = xr; fa.xi = xi; fa.yr = yr; fa.yi = yi;
     fa.chirp = p->chirp64; fa.H = p->H64;
     fa.batch = batch; fa.n = (int)p->n; fa.scale = sc;
+    fa.xr32 = io ? io->xr : nullptr; fa.xi32 = io ? io->xi : nullptr;
+    fa.yr32 = io ? io->yr : nullptr; fa.yi32 = io ? io->yi : nullptr;
     return launch_f64_blue_fused(p->sub64->logn, inv, fa, st);
   }
   double* ar = work;
   double* ai = work + (size_t)m * batch;
   double* sub_work = work + 2 * (size_t)m * batch;
-  cudaError_t e = launch_f64_blue_pre(xr, xi, p->chirp64, ar, ai, batch, p->n, m, inv, st);
+  cudaError_t e = launch_f64_blue_pre(xr, xi, io ? io->xr : nullptr, io ? io->xi : nullptr, p->chirp64, ar, ai, batch,
+                                      p->n, m, inv, st);
   if (e == cudaSuccess) e = run_f64_pow2(p->sub64, ar, ai, ar, ai, batch, false, 1.0, sub_work, st);
   if (e == cudaSuccess) e = launch_f64_blue_mul(ar, ai, p->H64, batch, m, inv, st);
   if (e == cudaSuccess) e = run_f64_pow2(p->sub64, ar, ai, ar, ai, batch, true, 1.0, sub_work, st);
-  if (e == cudaSuccess) e = launch_f64_blue_post(ar, ai, p->chirp64, yr, yi, batch, p->n, m, inv, sc, st);
+  if (e == cudaSuccess)
+    e = launch_f64_blue_post(ar, ai, p->chirp64, yr, yi, io ? io->yr : nullptr, io ? io->yi : nullptr, batch, p->n, m,
+                             inv, sc, st);
   return e;
 }
 
@@ -1451,6 +1473,35 @@ int trnfft_exec_c2c_f64(trnfft_plan_t plan, const double* in_re, const double* i
   cudaError_t e = run_f64(plan, in_re, in_im, out_re, out_im, batch, inverse != 0, static_cast<double*>(work),
                           reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_f64");
+  return TRNFFT_SUCCESS;
+}
+
+int trnfft_exec_c2c_f64_f32io(trnfft_plan_t plan, const float* in_re, const float* in_im, float* out_re,
+                              float* out_im, int64_t batch, int inverse, void* work, void* stream) {
+  if (!plan) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64_f32io: null plan");
+  if (batch < 0) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64_f32io: negative batch");
+  if (!plan->f64)
+    return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64_f32io: call trnfft_plan_enable_f64 on the plan first");
+  if (batch == 0) return TRNFFT_SUCCESS;
+  int rc = check_ptrs("exec_c2c_f64_f32io", {in_re, in_im, out_re, out_im}, 4);
+  if (rc) return rc;
+  const size_t b = (size_t)plan->n * (size_t)batch * sizeof(float);
+  const bool partial = (ranges_overlap(in_re, b, out_re, b) || ranges_overlap(in_re, b, out_im, b) ||
+                        ranges_overlap(in_im, b, out_re, b) || ranges_overlap(in_im, b, out_im, b)) &&
+                       !(in_re == out_re && in_im == out_im);
+  if (partial) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64_f32io: input and output planes partly overlap");
+  const int64_t wb = f64_work_bytes(plan, batch);
+  if (wb > 0) {
+    if (!work) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64_f32io: n=%lld needs a work area of %lld bytes",
+                           (long long)plan->n, (long long)wb);
+    if (!aligned(work, 16)) return fail(TRNFFT_INVALID_VALUE, "exec_c2c_f64_f32io: work area not 16-byte aligned");
+  }
+  DeviceGuard g(plan->device);
+  if (!g.ok) return fail(TRNFFT_CUDA_ERROR, "exec_c2c_f64_f32io: cannot select device %d", plan->device);
+  const F32IO io{in_re, in_im, out_re, out_im};
+  cudaError_t e = run_f64(plan, nullptr, nullptr, nullptr, nullptr, batch, inverse != 0, static_cast<double*>(work),
+                          reinterpret_cast<cudaStream_t>(stream), &io);
+  if (e != cudaSuccess) return cuda_fail(e, "exec_c2c_f64_f32io");
   return TRNFFT_SUCCESS;
 }
 

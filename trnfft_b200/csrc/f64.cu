@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
     double2 v = make_double2(0.0, 0.0);
     if (c < cn) {
       const long long off = s_in[c] + (long long)j * a.in_js;
-      v = make_double2(a.xr[off], a.xi[off]);
+      v = a.xr32 ? make_double2((double)a.xr32[off], (double)a.xi32[off]) : make_double2(a.xr[off], a.xi[off]);
     }
     sb[c * L + j] = v;
   }
@@ -181,8 +181,13 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
       v = cmul64(v, w);
     }
     const long long off = s_out[c] + (long long)k * a.out_ks;
-    a.yr[off] = v.x * a.scale;
-    a.yi[off] = v.y * a.scale;
+    if (a.yr32) {
+      a.yr32[off] = (float)(v.x * a.scale);
+      a.yi32[off] = (float)(v.y * a.scale);
+    } else {
+      a.yr[off] = v.x * a.scale;
+      a.yi[off] = v.y * a.scale;
+    }
   }
 }
 
@@ -226,6 +231,7 @@ cudaError_t upload_tw64(const double2* host_table) {
 // ---- Bluestein chirp stages (fp64) ------------------------------------------
 // a[b][j] = x[b][j] * chirp_j (conj for the inverse) for j < n, 0 for n <= j < m
 __global__ void k_f64_blue_pre(const double* __restrict__ xr, const double* __restrict__ xi,
+                               const float* __restrict__ xr32, const float* __restrict__ xi32,
                                const double2* __restrict__ chirp, double* __restrict__ ar, double* __restrict__ ai,
                                long long batch, long long n, long long m, int inv) {
   const long long total = batch * m;
@@ -236,7 +242,8 @@ __global__ void k_f64_blue_pre(const double* __restrict__ xr, const double* __re
     if (j < n) {
       double2 c = chirp[j];
       if (inv) c.y = -c.y;
-      v = cmul64(make_double2(xr[b * n + j], xi[b * n + j]), c);
+      const long long o = b * n + j;
+      v = cmul64(xr32 ? make_double2((double)xr32[o], (double)xi32[o]) : make_double2(xr[o], xi[o]), c);
     }
     ar[i] = v.x;
     ai[i] = v.y;
@@ -261,7 +268,8 @@ __global__ void k_f64_blue_mul(double* __restrict__ ar, double* __restrict__ ai,
 // y[b][j] = a[b][j] * chirp_j * scale for j < n
 __global__ void k_f64_blue_post(const double* __restrict__ ar, const double* __restrict__ ai,
                                 const double2* __restrict__ chirp, double* __restrict__ yr, double* __restrict__ yi,
-                                long long batch, long long n, long long m, int inv, double scale) {
+                                float* __restrict__ yr32, float* __restrict__ yi32, long long batch, long long n,
+                                long long m, int inv, double scale) {
   const long long total = batch * n;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -269,8 +277,13 @@ __global__ void k_f64_blue_post(const double* __restrict__ ar, const double* __r
     double2 c = chirp[j];
     if (inv) c.y = -c.y;
     const double2 v = cmul64(make_double2(ar[b * m + j], ai[b * m + j]), c);
-    yr[i] = v.x * scale;
-    yi[i] = v.y * scale;
+    if (yr32) {
+      yr32[i] = (float)(v.x * scale);
+      yi32[i] = (float)(v.y * scale);
+    } else {
+      yr[i] = v.x * scale;
+      yi[i] = v.y * scale;
+    }
   }
 }
 
@@ -282,9 +295,10 @@ static unsigned ew_blocks(long long total) {
   return (unsigned)(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
-cudaError_t launch_f64_blue_pre(const double* xr, const double* xi, const double2* chirp, double* ar, double* ai,
-                                long long batch, long long n, long long m, bool inv, cudaStream_t st) {
-  k_f64_blue_pre<<<ew_blocks(batch * m), 256, 0, st>>>(xr, xi, chirp, ar, ai, batch, n, m, inv ? 1 : 0);
+cudaError_t launch_f64_blue_pre(const double* xr, const double* xi, const float* xr32, const float* xi32,
+                                const double2* chirp, double* ar, double* ai, long long batch, long long n, long long m,
+                                bool inv, cudaStream_t st) {
+  k_f64_blue_pre<<<ew_blocks(batch * m), 256, 0, st>>>(xr, xi, xr32, xi32, chirp, ar, ai, batch, n, m, inv ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -295,8 +309,10 @@ cudaError_t launch_f64_blue_mul(double* ar, double* ai, const double2* H, long l
 }
 
 cudaError_t launch_f64_blue_post(const double* ar, const double* ai, const double2* chirp, double* yr, double* yi,
-                                 long long batch, long long n, long long m, bool inv, double scale, cudaStream_t st) {
-  k_f64_blue_post<<<ew_blocks(batch * n), 256, 0, st>>>(ar, ai, chirp, yr, yi, batch, n, m, inv ? 1 : 0, scale);
+                                 float* yr32, float* yi32, long long batch, long long n, long long m, bool inv,
+                                 double scale, cudaStream_t st) {
+  k_f64_blue_post<<<ew_blocks(batch * n), 256, 0, st>>>(ar, ai, chirp, yr, yi, yr32, yi32, batch, n, m, inv ? 1 : 0,
+                                                        scale);
   return cudaGetLastError();
 }
 
@@ -432,6 +448,19 @@ __device__ __forceinline__ double2 blue_h(const double2* H, int k, int m, bool i
   return h;
 }
 
+__device__ __forceinline__ double2 blue_load(const F64BlueArgs& a, long long o) {
+  return a.xr32 ? make_double2((double)a.xr32[o], (double)a.xi32[o]) : make_double2(a.xr[o], a.xi[o]);
+}
+__device__ __forceinline__ void blue_store(const F64BlueArgs& a, long long o, double2 v) {
+  if (a.yr32) {
+    a.yr32[o] = (float)(v.x * a.scale);
+    a.yi32[o] = (float)(v.y * a.scale);
+  } else {
+    a.yr[o] = v.x * a.scale;
+    a.yi[o] = v.y * a.scale;
+  }
+}
+
 // m <= 4096: C transforms per block (sequence c of the block is row blockIdx.x * C + c)
 template <int LOGM, bool INV>
 __global__ void __launch_bounds__(kF64Threads) k_f64_blue_small(F64BlueArgs a) {
@@ -445,8 +474,7 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_blue_small(F64BlueArgs a) {
     const int c = idx / M, j = idx % M;
     const long long r = r0 + c;
     double2 v = make_double2(0.0, 0.0);
-    if (j < n && r < a.batch)
-      v = cmul64(make_double2(a.xr[r * n + j], a.xi[r * n + j]), blue_chirp(a.chirp, j, INV));
+    if (j < n && r < a.batch) v = cmul64(blue_load(a, r * n + j), blue_chirp(a.chirp, j, INV));
     sb[idx] = v;
   }
   __syncthreads();
@@ -459,8 +487,7 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_blue_small(F64BlueArgs a) {
     const long long r = r0 + c;
     if (r >= a.batch) break;
     const double2 v = cmul64(sb[c * M + j], blue_chirp(a.chirp, j, INV));
-    a.yr[r * n + j] = v.x * a.scale;
-    a.yi[r * n + j] = v.y * a.scale;
+    blue_store(a, r * n + j, v);
   }
 }
 
@@ -477,7 +504,7 @@ __global__ void __launch_bounds__(R4 ? kF64Big4Threads : kF64BigThreads, 1) k_f6
   sincospi(2.0 / M, &s, &c);  // W_M = exp(-2 pi i / M)
   for (int j = threadIdx.x; j < M; j += NT) {
     double2 v = make_double2(0.0, 0.0);
-    if (j < n) v = cmul64(make_double2(a.xr[r * n + j], a.xi[r * n + j]), blue_chirp(a.chirp, j, INV));
+    if (j < n) v = cmul64(blue_load(a, r * n + j), blue_chirp(a.chirp, j, INV));
     sb[j] = v;
   }
   __syncthreads();
@@ -490,8 +517,7 @@ __global__ void __launch_bounds__(R4 ? kF64Big4Threads : kF64BigThreads, 1) k_f6
   else f64_fft_r2_big<LOGM, true>(sb, make_double2(c, s));
   for (int j = threadIdx.x; j < n; j += NT) {
     const double2 v = cmul64(sb[j], blue_chirp(a.chirp, j, INV));
-    a.yr[r * n + j] = v.x * a.scale;
-    a.yi[r * n + j] = v.y * a.scale;
+    blue_store(a, r * n + j, v);
   }
 }
 

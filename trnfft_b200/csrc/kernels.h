@@ -158,15 +158,22 @@ struct F64SeqArgs {
   unsigned long long tw_mask;
   long long tw_off;
   double scale;
+  // float32 input / output planes: when set they replace xr/xi (yr/yi), converted on load (store)
+  const float* xr32;
+  const float* xi32;
+  float* yr32;
+  float* yi32;
 };
 
 cudaError_t launch_f64_seq(int logl, bool inv, const F64SeqArgs& a, cudaStream_t st);
-cudaError_t launch_f64_blue_pre(const double* xr, const double* xi, const double2* chirp, double* ar, double* ai,
-                                long long batch, long long n, long long m, bool inv, cudaStream_t st);
+cudaError_t launch_f64_blue_pre(const double* xr, const double* xi, const float* xr32, const float* xi32,
+                                const double2* chirp, double* ar, double* ai, long long batch, long long n, long long m,
+                                bool inv, cudaStream_t st);
 cudaError_t launch_f64_blue_mul(double* ar, double* ai, const double2* H, long long batch, long long m, bool inv,
                                 cudaStream_t st);
 cudaError_t launch_f64_blue_post(const double* ar, const double* ai, const double2* chirp, double* yr, double* yi,
-                                 long long batch, long long n, long long m, bool inv, double scale, cudaStream_t st);
+                                 float* yr32, float* yi32, long long batch, long long n, long long m, bool inv,
+                                 double scale, cudaStream_t st);
 cudaError_t launch_f32_to_f64(const float* x, double* y, long long count, cudaStream_t st);
 cudaError_t launch_f64_to_f32(const double* x, float* y, long long count, cudaStream_t st);
 // Upload W_4096^i in double to the current device (f64.cu), once per device.
@@ -184,6 +191,10 @@ struct F64BlueArgs {
   long long batch;
   int n;
   double scale;
+  const float* xr32;  // float32 planes replacing xr/xi (yr/yi) when set
+  const float* xi32;
+  float* yr32;
+  float* yi32;
 };
 constexpr int kMaxF64BlueFusedLog = 13;
 cudaError_t launch_f64_blue_fused(int logm, bool inv, const F64BlueArgs& a, cudaStream_t st);
