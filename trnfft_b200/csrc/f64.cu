@@ -55,7 +55,8 @@ struct F64Geom {
   static constexpr int NB2 = C * L / 2;
   static constexpr int BPT4 = (NB4 + kF64Threads - 1) / kF64Threads;
   static constexpr int BPT2 = (NB2 + kF64Threads - 1) / kF64Threads;
-  static constexpr size_t smem = (size_t)C * L * sizeof(double2);
+  static constexpr int LP = L;  // sequence pitch in shared memory
+  static constexpr size_t smem = (size_t)C * LP * sizeof(double2);
 };
 
 template <int LOGL, bool INV>
@@ -73,7 +74,7 @@ __device__ __forceinline__ void f64_block_fft(double2* sb) {
       if (t < GM::NB4) {
         const int c = t / (L / 4), j = t % (L / 4);
 #pragma unroll
-        for (int r = 0; r < 4; ++r) v[q][r] = sb[c * L + j + r * (L / 4)];
+        for (int r = 0; r < 4; ++r) v[q][r] = sb[c * GM::LP + j + r * (L / 4)];
       }
     }
     __syncthreads();
@@ -95,7 +96,7 @@ __device__ __forceinline__ void f64_block_fft(double2* sb) {
       const double2 s13 = make_double2(a1.x + a3.x, a1.y + a3.y), d13 = make_double2(a1.x - a3.x, a1.y - a3.y);
       // forward: X1 = d02 - i d13, X3 = d02 + i d13; the inverse swaps the signs
       const double2 md13 = INV ? make_double2(-d13.y, d13.x) : make_double2(d13.y, -d13.x);
-      double2* y = sb + c * L;
+      double2* y = sb + c * GM::LP;
       const int base = ((j >> lns) << (lns + 2)) + k;
       y[base] = make_double2(s02.x + s13.x, s02.y + s13.y);
       y[base + ns] = make_double2(d02.x + md13.x, d02.y + md13.y);
@@ -113,8 +114,8 @@ __device__ __forceinline__ void f64_block_fft(double2* sb) {
       const int t = threadIdx.x + q * kF64Threads;
       if (t < GM::NB2) {
         const int c = t / (L / 2), j = t % (L / 2);
-        v[q][0] = sb[c * L + j];
-        v[q][1] = sb[c * L + j + L / 2];
+        v[q][0] = sb[c * GM::LP + j];
+        v[q][1] = sb[c * GM::LP + j + L / 2];
       }
     }
     __syncthreads();
@@ -127,8 +128,8 @@ __device__ __forceinline__ void f64_block_fft(double2* sb) {
       double2 a0 = v[q][0], a1 = v[q][1];
       if (ns > 1) a1 = cmul64(a1, tw64<INV>(k << (kTw64Log - lns - 1)));
       const int base = ((j >> lns) << (lns + 1)) + k;
-      sb[c * L + base] = make_double2(a0.x + a1.x, a0.y + a1.y);
-      sb[c * L + base + ns] = make_double2(a0.x - a1.x, a0.y - a1.y);
+      sb[c * GM::LP + base] = make_double2(a0.x + a1.x, a0.y + a1.y);
+      sb[c * GM::LP + base + ns] = make_double2(a0.x - a1.x, a0.y - a1.y);
     }
     __syncthreads();
   }
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
       const long long off = s_in[c] + (long long)j * a.in_js;
       v = a.xr32 ? make_double2((double)a.xr32[off], (double)a.xi32[off]) : make_double2(a.xr[off], a.xi[off]);
     }
-    sb[c * L + j] = v;
+    sb[c * GM::LP + j] = v;
   }
   __syncthreads();
   f64_block_fft<LOGL, INV>(sb);
@@ -173,7 +174,7 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
     int c, k;
     if (out_seq_fast) { c = idx % C; k = idx / C; } else { c = idx / L; k = idx % L; }
     if (c >= cn) continue;
-    double2 v = sb[c * L + k];
+    double2 v = sb[c * GM::LP + k];
     if (a.tw_hi) {
       const unsigned long long e = (s_tw[c] * (unsigned long long)k) & a.tw_mask;
       double2 w = cmul64(a.tw_hi[e >> a.tw_split], a.tw_lo[e & ((1ULL << a.tw_split) - 1)]);
@@ -327,6 +328,12 @@ cudaError_t launch_f64_blue_post(const double* ar, const double* ai, const doubl
 
 constexpr int kF64BigThreads = 512;
 
+// Shared-memory slot of point i in the 8192-point kernels: one double2 of padding after every 8,
+// so the strided radix-4 / radix-2 stores of the early passes (stride 4 ns double2) fall in
+// distinct bank groups (33.6 M bank conflicts per launch without it, n = 4093 batch 4096);
+// contiguous accesses stay contiguous within each group of 8 lanes.
+__device__ __forceinline__ int f64p(int i) { return i + (i >> 3); }
+
 // m = 8192 with 1024 threads: six radix-4 passes (2 butterflies of 4 values per thread) and a
 // final radix-2 pass (4 butterflies per thread), half the shared-memory traffic of radix 2
 constexpr int kF64Big4Threads = 1024;
@@ -346,7 +353,7 @@ __device__ __forceinline__ void f64_fft_r4_big(double2* sb, double2 w_half) {
     for (int q = 0; q < BPT4; ++q) {
       const int j = threadIdx.x + q * NT;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) v[q][r] = sb[j + r * (L / 4)];
+      for (int r = 0; r < 4; ++r) v[q][r] = sb[f64p(j + r * (L / 4))];
     }
     __syncthreads();
 #pragma unroll
@@ -364,10 +371,10 @@ __device__ __forceinline__ void f64_fft_r4_big(double2* sb, double2 w_half) {
       const double2 s13 = make_double2(a1.x + a3.x, a1.y + a3.y), d13 = make_double2(a1.x - a3.x, a1.y - a3.y);
       const double2 md13 = INV ? make_double2(-d13.y, d13.x) : make_double2(d13.y, -d13.x);
       const int base = ((j >> lns) << (lns + 2)) + k;
-      sb[base] = make_double2(s02.x + s13.x, s02.y + s13.y);
-      sb[base + ns] = make_double2(d02.x + md13.x, d02.y + md13.y);
-      sb[base + 2 * ns] = make_double2(s02.x - s13.x, s02.y - s13.y);
-      sb[base + 3 * ns] = make_double2(d02.x - md13.x, d02.y - md13.y);
+      sb[f64p(base)] = make_double2(s02.x + s13.x, s02.y + s13.y);
+      sb[f64p(base + ns)] = make_double2(d02.x + md13.x, d02.y + md13.y);
+      sb[f64p(base + 2 * ns)] = make_double2(s02.x - s13.x, s02.y - s13.y);
+      sb[f64p(base + 3 * ns)] = make_double2(d02.x - md13.x, d02.y - md13.y);
     }
     __syncthreads();
   }
@@ -378,8 +385,8 @@ __device__ __forceinline__ void f64_fft_r4_big(double2* sb, double2 w_half) {
 #pragma unroll
     for (int q = 0; q < BPT2; ++q) {
       const int j = threadIdx.x + q * NT;
-      v[q][0] = sb[j];
-      v[q][1] = sb[j + L / 2];
+      v[q][0] = sb[f64p(j)];
+      v[q][1] = sb[f64p(j + L / 2)];
     }
     __syncthreads();
 #pragma unroll
@@ -390,8 +397,8 @@ __device__ __forceinline__ void f64_fft_r4_big(double2* sb, double2 w_half) {
       if (k & 1) w = cmul64(w, w_half);
       const double2 a0 = v[q][0], a1 = cmul64(v[q][1], w);
       const int base = ((j >> lns) << (lns + 1)) + k;
-      sb[base] = make_double2(a0.x + a1.x, a0.y + a1.y);
-      sb[base + ns] = make_double2(a0.x - a1.x, a0.y - a1.y);
+      sb[f64p(base)] = make_double2(a0.x + a1.x, a0.y + a1.y);
+      sb[f64p(base + ns)] = make_double2(a0.x - a1.x, a0.y - a1.y);
     }
     __syncthreads();
   }
@@ -410,8 +417,8 @@ __device__ __forceinline__ void f64_fft_r2_big(double2* sb, double2 w_half) {
 #pragma unroll
     for (int q = 0; q < BPT; ++q) {
       const int j = threadIdx.x + q * kF64BigThreads;
-      v[q][0] = sb[j];
-      v[q][1] = sb[j + NB];
+      v[q][0] = sb[f64p(j)];
+      v[q][1] = sb[f64p(j + NB)];
     }
     __syncthreads();
 #pragma unroll
@@ -430,8 +437,8 @@ __device__ __forceinline__ void f64_fft_r2_big(double2* sb, double2 w_half) {
         a1 = cmul64(a1, w);
       }
       const int base = ((j >> lns) << (lns + 1)) + k;
-      sb[base] = make_double2(a0.x + a1.x, a0.y + a1.y);
-      sb[base + ns] = make_double2(a0.x - a1.x, a0.y - a1.y);
+      sb[f64p(base)] = make_double2(a0.x + a1.x, a0.y + a1.y);
+      sb[f64p(base + ns)] = make_double2(a0.x - a1.x, a0.y - a1.y);
     }
     __syncthreads();
   }
@@ -475,18 +482,21 @@ __global__ void __launch_bounds__(kF64Threads) k_f64_blue_small(F64BlueArgs a) {
     const long long r = r0 + c;
     double2 v = make_double2(0.0, 0.0);
     if (j < n && r < a.batch) v = cmul64(blue_load(a, r * n + j), blue_chirp(a.chirp, j, INV));
-    sb[idx] = v;
+    sb[c * GM::LP + j] = v;
   }
   __syncthreads();
   f64_block_fft<LOGM, false>(sb);
-  for (int idx = threadIdx.x; idx < C * M; idx += kF64Threads) sb[idx] = cmul64(sb[idx], blue_h(a.H, idx % M, M, INV));
+  for (int idx = threadIdx.x; idx < C * M; idx += kF64Threads) {
+    const int s = (idx / M) * GM::LP + idx % M;
+    sb[s] = cmul64(sb[s], blue_h(a.H, idx % M, M, INV));
+  }
   __syncthreads();
   f64_block_fft<LOGM, true>(sb);  // unscaled: 1/m is folded into H
   for (int idx = threadIdx.x; idx < C * n; idx += kF64Threads) {
     const int c = idx / n, j = idx % n;
     const long long r = r0 + c;
     if (r >= a.batch) break;
-    const double2 v = cmul64(sb[c * M + j], blue_chirp(a.chirp, j, INV));
+    const double2 v = cmul64(sb[c * GM::LP + j], blue_chirp(a.chirp, j, INV));
     blue_store(a, r * n + j, v);
   }
 }
@@ -505,18 +515,18 @@ __global__ void __launch_bounds__(R4 ? kF64Big4Threads : kF64BigThreads, 1) k_f6
   for (int j = threadIdx.x; j < M; j += NT) {
     double2 v = make_double2(0.0, 0.0);
     if (j < n) v = cmul64(blue_load(a, r * n + j), blue_chirp(a.chirp, j, INV));
-    sb[j] = v;
+    sb[f64p(j)] = v;
   }
   __syncthreads();
   if constexpr (R4) f64_fft_r4_big<LOGM, false>(sb, make_double2(c, -s));
   else f64_fft_r2_big<LOGM, false>(sb, make_double2(c, -s));
-  for (int k = threadIdx.x; k < M; k += NT) sb[k] = cmul64(sb[k], blue_h(a.H, k, M, INV));
+  for (int k = threadIdx.x; k < M; k += NT) sb[f64p(k)] = cmul64(sb[f64p(k)], blue_h(a.H, k, M, INV));
   __syncthreads();
   // unscaled inverse: 1/m is folded into H
   if constexpr (R4) f64_fft_r4_big<LOGM, true>(sb, make_double2(c, s));
   else f64_fft_r2_big<LOGM, true>(sb, make_double2(c, s));
   for (int j = threadIdx.x; j < n; j += NT) {
-    const double2 v = cmul64(sb[j], blue_chirp(a.chirp, j, INV));
+    const double2 v = cmul64(sb[f64p(j)], blue_chirp(a.chirp, j, INV));
     blue_store(a, r * n + j, v);
   }
 }
@@ -563,7 +573,7 @@ cudaError_t launch_f64_blue_fused(int logm, bool inv, const F64BlueArgs& a, cuda
       const bool r2 = f64_blue_r2();
       auto kern = r2 ? (inv ? k_f64_blue_big<true, false> : k_f64_blue_big<false, false>)
                      : (inv ? k_f64_blue_big<true, true> : k_f64_blue_big<false, true>);
-      const size_t smem = sizeof(double2) << 13;
+      const size_t smem = sizeof(double2) * ((1 << 13) + (1 << 10));  // padded (f64p)
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
       if (a.batch > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
