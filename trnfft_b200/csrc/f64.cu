@@ -86,11 +86,12 @@ __device__ __forceinline__ void f64_block_fft(double2* sb) {
       const int k = j & (ns - 1);
       double2 a0 = v[q][0], a1 = v[q][1], a2 = v[q][2], a3 = v[q][3];
       if (ns > 1) {
-        // W_{4 ns}^{k r} = W_4096^{k r 4096 / (4 ns)}
-        const int step = k << (kTw64Log - lns - 2);
-        a1 = cmul64(a1, tw64<INV>(step));
-        a2 = cmul64(a2, tw64<INV>(2 * step));
-        a3 = cmul64(a3, tw64<INV>(3 * step));
+        // W_{4 ns}^{k r} = W_4096^{k r 4096 / (4 ns)}: one table read, W^2k and W^3k by products
+        const double2 w1 = tw64<INV>(k << (kTw64Log - lns - 2));
+        const double2 w2 = cmul64(w1, w1);
+        a1 = cmul64(a1, w1);
+        a2 = cmul64(a2, w2);
+        a3 = cmul64(a3, cmul64(w2, w1));
       }
       const double2 s02 = make_double2(a0.x + a2.x, a0.y + a2.y), d02 = make_double2(a0.x - a2.x, a0.y - a2.y);
       const double2 s13 = make_double2(a1.x + a3.x, a1.y + a3.y), d13 = make_double2(a1.x - a3.x, a1.y - a3.y);
@@ -362,10 +363,12 @@ __device__ __forceinline__ void f64_fft_r4_big(double2* sb, double2 w_half) {
       const int k = j & (ns - 1);
       double2 a0 = v[q][0], a1 = v[q][1], a2 = v[q][2], a3 = v[q][3];
       if (ns > 1) {
-        const int step = k << (kTw64Log - lns - 2);  // W_{4 ns}^k = W_4096^(k 4096 / (4 ns)), lns <= 10
-        a1 = cmul64(a1, tw64<INV>(step));
-        a2 = cmul64(a2, tw64<INV>(2 * step));
-        a3 = cmul64(a3, tw64<INV>(3 * step));
+        // W_{4 ns}^k = W_4096^(k 4096 / (4 ns)), lns <= 10: one table read, W^2k and W^3k by products
+        const double2 w1 = tw64<INV>(k << (kTw64Log - lns - 2));
+        const double2 w2 = cmul64(w1, w1);
+        a1 = cmul64(a1, w1);
+        a2 = cmul64(a2, w2);
+        a3 = cmul64(a3, cmul64(w2, w1));
       }
       const double2 s02 = make_double2(a0.x + a2.x, a0.y + a2.y), d02 = make_double2(a0.x - a2.x, a0.y - a2.y);
       const double2 s13 = make_double2(a1.x + a3.x, a1.y + a3.y), d13 = make_double2(a1.x - a3.x, a1.y - a3.y);
