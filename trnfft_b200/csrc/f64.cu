@@ -137,7 +137,7 @@ __device__ __forceinline__ void f64_block_fft(double2* sb) {
 }
 
 template <int LOGL, bool INV>
-__global__ void __launch_bounds__(kF64Threads) k_f64_seq(F64SeqArgs a) {
+__global__ void __launch_bounds__(kF64Threads, 3) k_f64_seq(F64SeqArgs a) {
   using GM = F64Geom<LOGL>;
   constexpr int L = GM::L;
   constexpr int C = GM::C;
