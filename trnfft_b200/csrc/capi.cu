@@ -646,8 +646,10 @@ static int make_mixed_tables(trnfft_plan_s* p) {
   for (int q = 0; q < p->npass; ++q) {
     const int R = p->radix[q];
     p->codes |= (unsigned long long)mixed_code(R) << (3 * q);
-    for (long long k = 0; k < ns; ++k)
-      for (int r = 1; r < R; ++r) {
+    // block of pass q: entry (r - 1) * ns + k = W_{ns R}^{k r} (r-major: the butterflies of a
+    // warp, consecutive k, read consecutive entries for each r)
+    for (int r = 1; r < R; ++r)
+      for (long long k = 0; k < ns; ++k) {
         const long long e = (k * r) % (ns * R);
         const double a = -2.0 * M_PI * (double)e / (double)(ns * R);
         t.push_back(make_float2((float)std::cos(a), (float)std::sin(a)));

@@ -111,7 +111,8 @@ __device__ __forceinline__ void dft_any(float (&re)[R], float (&im)[R]) {
 // LAST: outputs to HBM through `st(i, re, im)`.  Middle passes load, transform
 // and store one butterfly at a time (the two buffers alternate), so a thread
 // holds only R values.  `twp` is this pass's twiddle block: entry
-// k*(R-1) + r-1 = W_{ns R}^{k r}, read contiguously by neighbouring butterflies.
+// (r-1)*ns + k = W_{ns R}^{k r}, so for each r the butterflies of a warp
+// (consecutive k) read consecutive entries.
 template <int R, bool INV, int LOGNMAX, bool FIRST, bool LAST, class Ld, class St>
 __device__ __forceinline__ void mix_pass(const float2* src, float2* dst, int j0, int n, int ns,
                                          const float2* __restrict__ twp, Ld ld, St st) {
@@ -122,10 +123,9 @@ __device__ __forceinline__ void mix_pass(const float2* src, float2* dst, int j0,
     const int hi = b / ns;
     const int k = b - hi * ns;
     if (ns > 1) {
-      const float2* w_ = twp + k * (R - 1);
 #pragma unroll
       for (int r = 1; r < R; ++r) {
-        float2 w = __ldg(w_ + r - 1);
+        float2 w = __ldg(twp + (r - 1) * ns + k);
         if (INV) w.y = -w.y;
         const float xr = vr[r], xi = vi[r];
         vr[r] = fmaf(xr, w.x, -xi * w.y);
