@@ -22,6 +22,7 @@
 namespace tfb {
 
 __device__ float2 g_tw[kTwN];
+__device__ float2 g_twd[kTwN];
 
 namespace {
 
@@ -45,7 +46,7 @@ constexpr int kMaxDevices = 64;
 std::mutex g_init_mu;
 bool g_dev_ready[kMaxDevices];
 
-// Upload the W_16384 table to `device` (once per device, that device current).
+// Upload the W_16384 table and the level tables to `device` (once per device, that device current).
 int ensure_device_tables(int device) {
   std::lock_guard<std::mutex> lk(g_init_mu);
   if (device < 0 || device >= kMaxDevices) return fail(TRNFFT_INVALID_VALUE, "device %d out of range", device);
@@ -57,6 +58,17 @@ int ensure_device_tables(int device) {
   }
   cudaError_t e = cudaMemcpyToSymbol(g_tw, h.data(), sizeof(float2) * kTwN);
   if (e != cudaSuccess) return cuda_fail(e, "uploading twiddle table");
+  // level tables D_L[k] = W_{2^L}^k, k < 2^(L-1), level L from offset 2^(L-1) - 1
+  std::vector<float2> hd(kTwN, make_float2(1.f, 0.f));
+  for (int L = 1; L <= kTwLog; ++L) {
+    const int off = (1 << (L - 1)) - 1;
+    for (int k = 0; k < (1 << (L - 1)); ++k) {
+      const double a = -2.0 * M_PI * (double)k / (double)(1 << L);
+      hd[off + k] = make_float2((float)std::cos(a), (float)std::sin(a));
+    }
+  }
+  e = cudaMemcpyToSymbol(g_twd, hd.data(), sizeof(float2) * kTwN);
+  if (e != cudaSuccess) return cuda_fail(e, "uploading the level twiddle tables");
   std::vector<double2> h64(4096);
   for (int i = 0; i < 4096; ++i) {
     const double a = -2.0 * M_PI * (double)i / 4096.0;

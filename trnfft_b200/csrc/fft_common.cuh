@@ -146,6 +146,12 @@ extern __device__ float2 g_tw[kTwN];
 
 __device__ __forceinline__ float2 tw_lookup(int idx) { return __ldg(&g_tw[idx]); }
 
+// Dense per-level tables D_L[k] = W_{2^L}^k for k < 2^(L-1), L = 1..14, level L stored from
+// offset 2^(L-1) - 1 (16383 entries).  A Stockham pass needs W_{NS R}^{k 2^t} = D_{LNS+LR-t}[k]
+// for consecutive k across a warp, so each of its table reads is contiguous.
+extern __device__ float2 g_twd[kTwN];
+__device__ __forceinline__ float2 tw_level(int L, int k) { return __ldg(&g_twd[(1 << (L - 1)) - 1 + k]); }
+
 // Shared memory holds complex values interleaved (one float2 per element, so
 // one 8-byte access moves a value) with one float2 of padding after every
 // 2^SH elements.  With SH = log2 of the largest radix, the stride-R writes of
@@ -219,8 +225,8 @@ __device__ __forceinline__ void pass_compute_store_qr(int j, float (&vr)[Sched<L
       ai[r] = vi[q * R + r];
     }
     if constexpr (NS > 1) {
-      // W_{NS*R}^{k*r} = W_16384^{(k*r) << (14 - LNS - LR)}.  The power-of-two
-      // exponents r = 1, 2, 4, ... come from the table; every other r is the
+      // W_{NS*R}^{k*r}.  The power-of-two exponents r = 2^t come from the level
+      // tables (W_{NS*R}^{k 2^t} = D_{LNS+LR-t}[k]); every other r is the
       // product of the twiddle of its highest set bit and an already formed
       // twiddle (at most popcount(r)-1 roundings deep).
       float wr[R], wi[R];
@@ -230,7 +236,7 @@ __device__ __forceinline__ void pass_compute_store_qr(int j, float (&vr)[Sched<L
       for (int r = 1; r < R; ++r) {
         const int hb = 1 << (31 - __clz(r));
         if (hb == r) {
-          const float2 w = tw_lookup((k * r) << (kTwLog - LNS - LR));
+          const float2 w = tw_level(LNS + LR - (31 - __clz(r)), k);
           wr[r] = w.x;
           wi[r] = INV ? -w.y : w.y;
         } else {
