@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(IstftGeom<LOGM, TB>::THREADS, IstftGeom<LOGM, 
         const float br = tre[km * GM::TP + g], bi = (km == M) ? 0.f : tim[km * GM::TP + g];
         const float er = ar + br, ei = ai - bi;
         const float dr = ar - br, di = ai + bi;
-        const float2 tw = tw_lookup(k << (kTwLog - LOGN));
+        const float2 tw = tw_level(LOGN, k);  // W_N^k, k < M = 2^(LOGN-1)
         const float orr = dr * tw.x + di * tw.y;
         const float oi = di * tw.x - dr * tw.y;
         r = er - oi;
